@@ -1,0 +1,453 @@
+"""Benchmark of MiniServe's per-step paged-attention path on B200.
+
+Workload (config 2 of the path's benchmark set): one decode step of Qwen3-0.6B's attention path
+over all 28 layers for 256 sequences with context lengths U[256, 4096] (one new token each),
+16 query / 8 KV heads, head_dim 128, 16-token blocks, a KV pool of 1.1x the blocks needed per
+layer with randomly permuted block tables, N(0,1) bf16 values (synthetic; no model weights are
+involved on this path).  A "step" = for each of the 28 layers: kernel A (q/k RMSNorm + RoPE +
+K/V scatter) and kernels B/C (paged split-KV attention + combine).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+With N > 1 (launched by torchrun) every rank runs its own config-2 batch on its own GPU
+(sequences shard across GPUs with no data-path collective: weak scaling); the time is the max
+over ranks.  ``--impl reference`` times the reference algorithm (the CPU oracle restating
+MiniServe's torch code) on the host cores instead.
+
+Rank 0 prints one JSON line.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+LAYERS = 28
+H, KVH, D = 16, 8, 128
+METRIC = "decode tok/s (paged-attn path, 28 layers, config 2)"
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+
+def parse() -> argparse.Namespace:
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--seqs", type=int, default=256)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--pages-per-split", type=int, default=0)
+    return p.parse_args()
+
+
+def peaks() -> tuple[dict, str]:
+    f = ROOT / "MEASURED_PEAKS.json"
+    if f.exists():
+        return json.loads(f.read_text()), "measured"
+    return PEAKS_FALLBACK, "fallback"
+
+
+# ---------------------------------------------------------------------------------------------
+# clocks sampled during the timed region
+# ---------------------------------------------------------------------------------------------
+
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int) -> None:
+        self.gpu = gpu_index
+        self.proc: subprocess.Popen | None = None
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+
+    def start(self) -> None:
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=self.file, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.file.flush()
+        rows = [r.split(",") for r in Path(self.file.name).read_text().splitlines() if r.strip()]
+        os.unlink(self.file.name)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                mx.append(float(r[2]))
+            except (ValueError, IndexError):
+                continue
+            for name, val in zip(names, r[5:9]):
+                if val.strip().lower() == "active":
+                    reasons.add(name)
+        return {
+            "sm_mhz": statistics.median(sm) if sm else None,
+            "sm_max_mhz": max(mx) if mx else None,
+            "reasons": sorted(reasons),
+            "samples": len(sm),
+        }
+
+
+# ---------------------------------------------------------------------------------------------
+# our implementation
+# ---------------------------------------------------------------------------------------------
+
+
+def attention_bytes(batch) -> tuple[int, int]:
+    """Algorithmic bytes of one attention launch (kernels B+C) and of one kernel-A launch.
+
+    Attention: every context token's K and V of each KV head once (bf16), the queries in and the
+    outputs out, and the block-table entries.  Kernel A: the qkv row read, q written, K and V
+    written to the pool, cos/sin rows and the slot/position indices.
+    """
+    ctx = sum(c.context_len for c in batch.chunks)
+    t = batch.num_tokens
+    tables = sum(-(-c.context_len // 16) for c in batch.chunks)
+    attn = ctx * KVH * D * 2 * 2 + t * H * D * 2 * 2 + tables * 4
+    kern_a = t * (H + 2 * KVH) * D * 2 + t * H * D * 2 + t * 2 * KVH * D * 2 + t * D * 4 * 2 + t * 8
+    return attn, kern_a
+
+
+def run_ours(args: argparse.Namespace, rank: int, world: int, device: torch.device) -> dict:
+    from miniserve_b200 import _capi
+    from miniserve_b200.attention import attend, build_attention_metadata
+    from miniserve_b200.kv_pool import allocate_kv_cache
+    from miniserve_b200.qwen3_attention import qk_norm_rope_scatter
+    from miniserve_b200.workloads import config2, rope_tables
+
+    batch = config2(seed=1000 + rank, num_seqs=args.seqs)
+    t = batch.num_tokens
+    g = torch.Generator(device=device).manual_seed(1234 + rank)
+    pool, views = allocate_kv_cache(LAYERS, batch.num_blocks, KVH, device, zero=False)
+    for layer in range(LAYERS):
+        pool[layer].normal_(generator=g)
+    qkv_all = torch.randn(LAYERS, t, (H + 2 * KVH) * D, generator=g, device=device,
+                          dtype=torch.bfloat16)
+    qw = (1 + 0.1 * torch.randn(LAYERS, D, generator=g, device=device)).bfloat16()
+    kw = (1 + 0.1 * torch.randn(LAYERS, D, generator=g, device=device)).bfloat16()
+    cos_t, sin_t = rope_tables(D, batch.max_position + 8, 1e6, device)
+    positions = torch.from_numpy(batch.positions).to(device)
+    slot_mapping = torch.from_numpy(batch.slots).to(device)
+    cos, sin = cos_t[positions], sin_t[positions]
+    meta = build_attention_metadata(batch.chunks, slot_mapping, 16,
+                                    pages_per_split=args.pages_per_split)
+    q_buf = torch.empty(t, H, D, dtype=torch.bfloat16, device=device)
+    out_all = torch.empty(LAYERS, t, H, D, dtype=torch.bfloat16, device=device)
+    stream = torch.cuda.current_stream(device)
+    scale = D**-0.5
+    info = meta.info
+    launches_per_layer = 1 + (info.n_decode_items > 0) + (info.n_tile_items > 0) + (info.n_combine > 0)
+
+    ev_attn = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(LAYERS)]
+
+    def step(timed_kernels: bool = False) -> None:
+        for layer in range(LAYERS):
+            k_cache, v_cache = views[layer]
+            qk_norm_rope_scatter(qkv_all[layer], qw[layer], kw[layer], 1e-6, cos, sin,
+                                 slot_mapping, k_cache, v_cache, H, q_out=q_buf)
+            if timed_kernels:
+                ev_attn[layer][0].record(stream)
+            attend(q_buf, k_cache, v_cache, meta, scale, out=out_all[layer])
+            if timed_kernels:
+                ev_attn[layer][1].record(stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(device)
+    status = _capi.device_status(int(stream.cuda_stream))
+    if status:
+        raise RuntimeError(f"device status {status:#x} after warm-up")
+
+    # ---- timed region: device-resident inputs ----
+    sampler = ClockSampler(device.index if device.index is not None else 0) if rank == 0 else None
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize(device)
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    attn_ms: list[float] = []
+    start.record(stream)
+    for _ in range(args.steps):
+        step(timed_kernels=False)
+    stop.record(stream)
+    torch.cuda.synchronize(device)
+    total_ms = start.elapsed_time(stop)
+    # per-kernel durations (same work, events around each attention launch)
+    for _ in range(max(1, min(args.steps, 5))):
+        step(timed_kernels=True)
+        torch.cuda.synchronize(device)
+        attn_ms.extend(ev_attn[layer][0].elapsed_time(ev_attn[layer][1]) for layer in range(LAYERS))
+    clocks = sampler.stop() if sampler else None
+    if world > 1:
+        torch.distributed.barrier()
+    status = _capi.device_status(int(stream.cuda_stream))
+    if status:
+        raise RuntimeError(f"device status {status:#x} after timing")
+
+    # ---- e2e: through the public API with host buffers ----
+    qkv_host = qkv_all.cpu().pin_memory()
+    out_host = torch.empty(LAYERS, t, H, D, dtype=torch.bfloat16).pin_memory()
+    pos_host = torch.from_numpy(batch.positions).pin_memory()
+    slot_host = torch.from_numpy(batch.slots).pin_memory()
+    qkv_dev = torch.empty_like(qkv_all)
+
+    def e2e_step() -> None:
+        slots_d = slot_host.to(device, non_blocking=True)
+        pos_d = pos_host.to(device, non_blocking=True)
+        m = build_attention_metadata(batch.chunks, slots_d, 16, pages_per_split=args.pages_per_split)
+        qkv_dev.copy_(qkv_host, non_blocking=True)
+        c, s = cos_t[pos_d], sin_t[pos_d]
+        for layer in range(LAYERS):
+            k_cache, v_cache = views[layer]
+            q = qk_norm_rope_scatter(qkv_dev[layer], qw[layer], kw[layer], 1e-6, c, s, slots_d,
+                                     k_cache, v_cache, H, q_out=q_buf)
+            attend(q, k_cache, v_cache, m, scale, out=out_all[layer])
+        out_host.copy_(out_all, non_blocking=True)
+
+    for _ in range(max(1, args.warmup)):
+        e2e_step()
+    torch.cuda.synchronize(device)
+    if world > 1:
+        torch.distributed.barrier()
+    e_start, e_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_start.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e_stop.record(stream)
+    torch.cuda.synchronize(device)
+    e2e_ms = e_start.elapsed_time(e_stop)
+    h2d = qkv_host.numel() * 2 + pos_host.numel() * 8 + slot_host.numel() * 8 + int(info.total_ints) * 4
+    d2h = out_host.numel() * 2
+
+    attn_bytes, a_bytes = attention_bytes(batch)
+    return {
+        "total_ms": total_ms,
+        "e2e_ms": e2e_ms,
+        "attn_ms": float(np.mean(attn_ms)),
+        "attn_bytes": attn_bytes,
+        "kernel_a_bytes": a_bytes,
+        "tokens": t,
+        "kv_tokens": batch.kv_tokens_read(),
+        "num_blocks": batch.num_blocks,
+        "clocks": clocks,
+        "launches_per_step": LAYERS * launches_per_layer,
+        "h2d": h2d,
+        "d2h": d2h,
+        "plan": {"decode_items": info.n_decode_items, "tile_items": info.n_tile_items,
+                 "combine": info.n_combine, "pages_per_split": info.pages_per_split},
+    }
+
+
+# ---------------------------------------------------------------------------------------------
+# the reference's CPU path (oracle restatement of MiniServe's torch code)
+# ---------------------------------------------------------------------------------------------
+
+
+def cpu_reference_layer_setup(num_seqs: int, seed: int = 0):
+    """One layer of config 2 in the reference's own layout and dtype, on the host."""
+    from miniserve_b200.workloads import config2
+    from oracle import attention_oracle as orc
+
+    batch = config2(seed=seed, num_seqs=num_seqs)
+    # Compact pool: only the blocks the batch uses, renumbered densely (same geometry).
+    used = sorted({b for c in batch.chunks for b in c.block_table})
+    remap = {b: i for i, b in enumerate(used)}
+    chunks = [orc.SeqChunk(c.flat_start, c.num_new, c.num_cached, [remap[b] for b in c.block_table])
+              for c in batch.chunks]
+    g = torch.Generator().manual_seed(seed)
+    nslots = len(used) * 16
+    t = batch.num_tokens
+    k_cache = torch.randn(nslots, KVH, D, generator=g).bfloat16()
+    v_cache = torch.randn(nslots, KVH, D, generator=g).bfloat16()
+    qkv = torch.randn(t, (H + 2 * KVH) * D, generator=g).bfloat16()
+    qw = (1 + 0.1 * torch.randn(D, generator=g)).bfloat16()
+    kw = (1 + 0.1 * torch.randn(D, generator=g)).bfloat16()
+    cos, sin = orc.rope_tables(D, batch.max_position + 8, 1e6)
+    slots = torch.tensor([s for c in chunks for s in orc.slots_for(c, 16)], dtype=torch.long)
+    positions = torch.tensor([p for c in chunks for p in range(c.num_cached, c.context_len)],
+                             dtype=torch.long)
+
+    def layer() -> None:
+        meta = orc.build_metadata(chunks, slots, 16)
+        orc.attention_layer(qkv, qw, kw, 1e-6, cos, sin, positions, k_cache, v_cache, meta)
+
+    return layer, t
+
+
+def run_cpu_layers(num_seqs: int, warmup: int, iters: int | None, budget_s: float | None):
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    layer, t = cpu_reference_layer_setup(num_seqs)
+    for _ in range(warmup):
+        layer()
+    times = []
+    t_end = time.perf_counter() + (budget_s or 0)
+    while True:
+        t0 = time.perf_counter()
+        layer()
+        times.append(time.perf_counter() - t0)
+        if iters is not None and len(times) >= iters:
+            break
+        if budget_s is not None and time.perf_counter() >= t_end:
+            break
+    return float(np.mean(times)), t, threads, len(times)
+
+
+# ---------------------------------------------------------------------------------------------
+
+
+def main() -> None:
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        t_layer, t, threads, n = run_cpu_layers(args.seqs, args.warmup, args.steps, None)
+        value = t / (LAYERS * t_layer)
+        line = {
+            "impl": "reference",
+            "metric": METRIC,
+            "value": value,
+            "unit": "tok/s",
+            "n_gpus": args.gpus,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": t_layer * LAYERS * 1e3,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic",
+            "config": {"workload": f"config2: {args.seqs} decode seqs, ctx U[256,4096], 28 layers",
+                       "parallelism": "host cores"},
+            "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port",
+                             "sample": "each step = 1 of 28 layers of the full batch, on the "
+                                       "host CPU, time x28 (oracle restating MiniServe's torch "
+                                       "path)"},
+            "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0},
+        }
+        print(json.dumps(line), flush=True)
+        return
+
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py needs a CUDA GPU")
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if world > 1:
+        import datetime
+
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=device)
+    from miniserve_b200.build import build
+
+    if rank == 0:
+        build()
+    if world > 1:
+        torch.distributed.barrier()
+
+    r = run_ours(args, rank, world, device)
+    ms = torch.tensor([r["total_ms"], r["e2e_ms"], r["attn_ms"]], dtype=torch.float64,
+                      device=device)
+    if world > 1:
+        torch.distributed.all_reduce(ms, op=torch.distributed.ReduceOp.MAX)
+    total_ms, e2e_ms, attn_ms = (float(x) for x in ms.cpu())
+    ms_per_step = total_ms / args.steps
+    e2e_per_step = e2e_ms / args.steps
+    tokens_all = r["tokens"] * world
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        t_layer, t, threads, n = run_cpu_layers(args.seqs, 1, None, 12.0)
+        cpu = {"value": t / (LAYERS * t_layer), "unit": "tok/s", "cores": threads, "kind": "port",
+               "sample": f"1 of 28 layers of the full config-2 batch, {n} timed runs on the host "
+                         "CPU (oracle restating MiniServe's torch path), time x28"}
+
+    if rank == 0:
+        pk, src = peaks()
+        hbm = float(pk["hbm_gbs"])
+        achieved = r["attn_bytes"] / (attn_ms * 1e-3) / 1e9
+        traffic_file = ROOT / "profiles" / "traffic.json"
+        traffic = None
+        if traffic_file.exists():
+            traffic = json.loads(traffic_file.read_text()).get("paged_attn_decode_cfg2")
+        line = {
+            "metric": METRIC,
+            "value": tokens_all / (ms_per_step * 1e-3),
+            "unit": "tok/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": ms_per_step,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic",
+            "config": {
+                "workload": f"config2: {args.seqs} decode seqs/GPU, ctx U[256,4096], 16q/8kv "
+                            "heads, d128, block 16, 28 layers",
+                "kv_tokens_per_layer": r["kv_tokens"],
+                "pool_blocks_per_layer": r["num_blocks"],
+                "l2": "inputs larger than L2 (KV read per layer-step >> 126 MB)",
+                "parallelism": f"sequence-sharded x{world}, no data-path collective",
+            },
+            "us_per_layer_step": ms_per_step * 1e3 / LAYERS,
+            "attn_us_per_layer": attn_ms * 1e3,
+            "roofline": {
+                "kernel": "paged attention decode (kernel B + combine C)",
+                "bound": "hbm",
+                "achieved": achieved,
+                "peak": hbm,
+                "peak_source": src,
+                "unit": "GB/s",
+                "frac": achieved / hbm,
+                "traffic": traffic,
+                "algorithmic_bytes_per_launch": r["attn_bytes"],
+            },
+            "cpu_baseline": cpu,
+            "e2e": {"value": tokens_all / (e2e_per_step * 1e-3), "unit": "tok/s",
+                    "h2d_bytes_per_step": r["h2d"], "d2h_bytes_per_step": r["d2h"]},
+            "gpu_launches": r["launches_per_step"] * args.steps,
+            "clocks": r["clocks"],
+            "plan": r["plan"],
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,197 @@
+"""Drop-in replacement for MiniServe's attention backend (src/miniserve/attention/backends.py).
+
+Same names and call shapes as the reference module:
+
+* ``SeqChunk(flat_start, num_new, num_cached, block_table)``            (backends.py:36-47)
+* ``build_attention_metadata(chunks, slot_mapping, block_size)``       (backends.py:80-98)
+* ``paged_attention(q, k, v, k_cache, v_cache, meta, scale) -> [T, H, D]`` (backends.py:145-197)
+* ``SHORT_QUERY`` and ``MAX_GATHER_TOKENS`` (backends.py:32-33; the runner's profiler imports the
+  latter, model_runner.py:21,111).
+
+What changes underneath: the metadata is one packed int32 plan built by the native planner and
+uploaded with a single pinned, non-blocking copy; the KV pool uses the layout of
+``miniserve_b200.kv_pool``; the scatter and the attention are hand-written sm_100a kernels that
+read the pool in place (no gather copy, no padding, no masks in memory).  Everything runs on the
+caller's current CUDA stream and never synchronises; errors surface as ``ValueError`` /
+``RuntimeError`` like the reference's.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass, field
+from itertools import chain
+
+import numpy as np
+import torch
+from torch import Tensor
+
+from . import _capi
+from .kv_pool import BLOCK_SIZE, HEAD_DIM, check_layer_views
+
+SHORT_QUERY = 8  # rows with at most this many new tokens take the decode kernel
+MAX_GATHER_TOKENS = 16384  # kept for the runner's profiler; nothing is gathered here
+
+
+@dataclass
+class SeqChunk:
+    """What attention needs to know about one scheduled sequence (backends.py:36-47)."""
+
+    flat_start: int  # where its new tokens start in the flattened batch
+    num_new: int  # new tokens this step (its queries)
+    num_cached: int  # tokens already in the KV cache before this step
+    block_table: list[int]
+
+    @property
+    def context_len(self) -> int:
+        return self.num_cached + self.num_new
+
+
+@dataclass
+class AttentionMetadata:
+    """The per-step plan, built once and shared by every layer (backends.py:67-71)."""
+
+    slot_mapping: Tensor  # [T] int64 slot of each new token, on the device
+    plan: Tensor  # packed int32 plan on the device
+    info: _capi.MsPlanInfo  # host-side description of the plan
+    num_tokens: int
+    _workspace: dict[tuple[int, int], Tensor] = field(default_factory=dict, repr=False)
+
+    def workspace(self, num_kv_heads: int, device: torch.device) -> Tensor | None:
+        """Split-KV scratch for this step (allocated once, reused by every layer)."""
+        need = int(self.info.workspace_bytes_per_kv_head) * num_kv_heads
+        if need == 0:
+            return None
+        key = (device.index if device.index is not None else torch.cuda.current_device(), num_kv_heads)
+        ws = self._workspace.get(key)
+        if ws is None:
+            ws = torch.empty(need, dtype=torch.uint8, device=device)
+            self._workspace[key] = ws
+        return ws
+
+
+_SM_COUNT: dict[int, int] = {}
+
+
+def _num_sms(device: torch.device) -> int:
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    if idx not in _SM_COUNT:
+        _SM_COUNT[idx] = torch.cuda.get_device_properties(idx).multi_processor_count
+    return _SM_COUNT[idx]
+
+
+def plan_batch(
+    chunks: list[SeqChunk],
+    num_tokens: int,
+    block_size: int = BLOCK_SIZE,
+    num_sms: int = 148,
+    pages_per_split: int = 0,
+) -> tuple[np.ndarray, _capi.MsPlanInfo]:
+    """Run the native planner on the host; returns ``(packed int32 plan, info)``."""
+    lib = _capi.load()
+    n = len(chunks)
+    flat = np.fromiter((c.flat_start for c in chunks), dtype=np.int32, count=n)
+    new = np.fromiter((c.num_new for c in chunks), dtype=np.int32, count=n)
+    cached = np.fromiter((c.num_cached for c in chunks), dtype=np.int32, count=n)
+    lens = np.fromiter((len(c.block_table) for c in chunks), dtype=np.int64, count=n)
+    offsets = np.zeros(n + 1, dtype=np.int64)
+    np.cumsum(lens, out=offsets[1:])
+    total = int(offsets[-1])
+    tables = np.fromiter(chain.from_iterable(c.block_table for c in chunks), dtype=np.int32,
+                         count=total)
+    cap = int(lib.ms_plan_capacity(n, num_tokens, total))
+    out = np.empty(cap, dtype=np.int32)
+    info = _capi.MsPlanInfo()
+    rc = lib.ms_plan_build(
+        n, flat.ctypes.data, new.ctypes.data, cached.ctypes.data, offsets.ctypes.data,
+        tables.ctypes.data if total else None, num_tokens, block_size, num_sms, pages_per_split,
+        out.ctypes.data, cap, C.byref(info),
+    )
+    _capi.check(rc, "build_attention_metadata")
+    return out[: info.total_ints], info
+
+
+def build_attention_metadata(
+    chunks: list[SeqChunk],
+    slot_mapping: Tensor,
+    block_size: int,
+    *,
+    pages_per_split: int = 0,
+) -> AttentionMetadata:
+    """Plan one step and upload it (one pinned H2D copy, no sync).  backends.py:80-98."""
+    device = slot_mapping.device
+    if device.type != "cuda":
+        raise RuntimeError("miniserve_b200 attention runs on CUDA only (no CPU fallback)")
+    if block_size != BLOCK_SIZE:
+        raise ValueError(f"block_size must be {BLOCK_SIZE}")
+    num_tokens = int(slot_mapping.shape[0])
+    packed, info = plan_batch(chunks, num_tokens, block_size, _num_sms(device), pages_per_split)
+    host = torch.from_numpy(packed).pin_memory()
+    plan = host.to(device, non_blocking=True)
+    slots = slot_mapping if slot_mapping.dtype == torch.int64 else slot_mapping.to(torch.int64)
+    return AttentionMetadata(slots.contiguous(), plan, info, num_tokens)
+
+
+def _stream(device: torch.device) -> int:
+    return int(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _rows(t: Tensor, name: str) -> int:
+    """Row stride (elements) of a [T, heads, 128] tensor whose heads are packed in each row."""
+    if t.dim() != 3 or t.shape[2] != HEAD_DIM or t.stride(2) != 1 or t.stride(1) != HEAD_DIM:
+        raise ValueError(f"{name} must be [T, heads, {HEAD_DIM}] with contiguous heads")
+    if t.dtype != torch.bfloat16:
+        raise ValueError(f"{name} must be bf16")
+    return int(t.stride(0))
+
+
+def kv_scatter(k: Tensor, v: Tensor, slot_mapping: Tensor, k_cache: Tensor, v_cache: Tensor) -> None:
+    """Write this step's K/V rows into their slots (backends.py:159-160)."""
+    nb, kvh = check_layer_views(k_cache, v_cache)
+    t = int(k.shape[0])
+    lib = _capi.load()
+    rc = lib.ms_kv_scatter(
+        k.data_ptr(), _rows(k, "k"), v.data_ptr(), _rows(v, "v"), t, kvh,
+        slot_mapping.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), nb, _stream(k.device),
+    )
+    _capi.check(rc, "kv_scatter")
+
+
+def attend(q: Tensor, k_cache: Tensor, v_cache: Tensor, meta: AttentionMetadata, scale: float,
+           out: Tensor | None = None) -> Tensor:
+    """Attention of every planned query row through the pool (backends.py:161-197).
+
+    Rows not covered by ``meta`` are left untouched (undefined, like ``torch.empty_like``).
+    """
+    nb, kvh = check_layer_views(k_cache, v_cache)
+    if out is None:
+        out = torch.empty_like(q)
+    h = int(q.shape[1])
+    ws = meta.workspace(kvh, q.device)
+    lib = _capi.load()
+    rc = lib.ms_paged_attention(
+        q.data_ptr(), _rows(q, "q"), out.data_ptr(), _rows(out, "out"), h, kvh,
+        k_cache.data_ptr(), v_cache.data_ptr(), nb, meta.plan.data_ptr(), C.byref(meta.info),
+        ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0,
+        float(scale), _stream(q.device),
+    )
+    _capi.check(rc, "paged_attention")
+    return out
+
+
+def paged_attention(
+    q: Tensor,
+    k: Tensor,
+    v: Tensor,
+    k_cache: Tensor,
+    v_cache: Tensor,
+    meta: AttentionMetadata,
+    scale: float,
+) -> Tensor:
+    """Write this step's keys and values into the cache, then attend through it.
+
+    q: [T, heads, 128]; k, v: [T, kv_heads, 128]; caches: layer views of the pool.
+    Returns [T, heads, 128] (backends.py:145-158).
+    """
+    kv_scatter(k, v, meta.slot_mapping, k_cache, v_cache)
+    return attend(q, k_cache, v_cache, meta, scale)

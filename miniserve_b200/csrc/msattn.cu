@@ -1,0 +1,393 @@
+// C-ABI entry points of libmsattn.so (declared in include/msattn.h).
+//
+// This translation unit owns the kernels (included below), the per-thread error string, the
+// tensor-map cache for KV pools and the launch logic.  Nothing here allocates device memory or
+// synchronises a stream, except ms_device_status.
+#include <cudaTypedefs.h>
+
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+
+#include "../../include/msattn.h"
+#include "ms_common.cuh"
+#include "norm_rope_scatter.cuh"
+#include "paged_attention.cuh"
+
+namespace ms_host {
+
+thread_local std::string g_last_error;
+
+void set_error(const std::string& msg) { g_last_error = msg; }
+
+static int cuda_fail(const char* what, cudaError_t e) {
+  set_error(std::string(what) + ": " + cudaGetErrorName(e) + " (" + cudaGetErrorString(e) + ")");
+  return MS_ERR_CUDA;
+}
+
+// ---- TMA descriptors for KV pools -----------------------------------------------------------
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+struct MapKey {
+  int device;
+  uintptr_t base;
+  int num_blocks;
+  int num_kv;
+  bool operator==(const MapKey& o) const {
+    return device == o.device && base == o.base && num_blocks == o.num_blocks && num_kv == o.num_kv;
+  }
+};
+struct MapKeyHash {
+  size_t operator()(const MapKey& k) const {
+    return std::hash<uintptr_t>()(k.base) ^ (static_cast<size_t>(k.num_blocks) << 20) ^
+           (static_cast<size_t>(k.device) << 56) ^ static_cast<size_t>(k.num_kv);
+  }
+};
+
+static std::mutex g_map_mutex;
+static std::unordered_map<MapKey, CUtensorMap, MapKeyHash> g_maps;
+
+// One layer's pool region viewed as a 5-D tensor {64 dims, 16 tokens, 4 quarters (K lo, K hi,
+// V lo, V hi), KV heads, blocks}; one box is a whole 8 KiB (block, head) page pair.
+static int kv_tensor_map(const void* k_cache, int num_blocks, int num_kv, CUtensorMap* out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail("cudaGetDevice", e);
+  const MapKey key{dev, reinterpret_cast<uintptr_t>(k_cache), num_blocks, num_kv};
+  std::lock_guard<std::mutex> lock(g_map_mutex);
+  auto it = g_maps.find(key);
+  if (it != g_maps.end()) {
+    *out = it->second;
+    return MS_OK;
+  }
+  auto fn = encode_fn();
+  if (fn == nullptr) {
+    set_error("cuTensorMapEncodeTiled is unavailable from the driver");
+    return MS_ERR_CUDA;
+  }
+  const cuuint64_t dims[5] = {64, 16, 4, static_cast<cuuint64_t>(num_kv),
+                              static_cast<cuuint64_t>(num_blocks)};
+  const cuuint64_t strides[4] = {128, 2048, ms::kPageKVBytes,
+                                 static_cast<cuuint64_t>(num_kv) * ms::kPageKVBytes};
+  const cuuint32_t box[5] = {64, 16, 4, 1, 1};
+  const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  CUtensorMap map;
+  const CUresult r = fn(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, const_cast<void*>(k_cache), dims,
+                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled failed with CUresult " + std::to_string(static_cast<int>(r)));
+    return MS_ERR_CUDA;
+  }
+  if (g_maps.size() > 4096) g_maps.clear();
+  g_maps.emplace(key, map);
+  *out = map;
+  return MS_OK;
+}
+
+// ---- attention launch configurations --------------------------------------------------------
+
+constexpr int kDecodeWarps = 4, kDecodeStages = 8;
+constexpr int kTileWarps = 8, kTileStages = 8;
+using DecodeCfg = ms::AttnCfg<0, kDecodeWarps, kDecodeStages>;
+using TileCfg = ms::AttnCfg<1, kTileWarps, kTileStages>;
+
+static int ensure_smem_attrs() {
+  // Per device: the attribute is a property of the function on the current device.
+  static std::mutex mu;
+  static bool done[64] = {false};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail("cudaGetDevice", e);
+  if (dev < 0 || dev >= 64) return MS_ERR_ARG;
+  std::lock_guard<std::mutex> lock(mu);
+  if (done[dev]) return MS_OK;
+  e = cudaFuncSetAttribute(ms::paged_attn_kernel<0, kDecodeWarps, kDecodeStages>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, DecodeCfg::kSmemBytes);
+  if (e != cudaSuccess) return cuda_fail("cudaFuncSetAttribute(decode)", e);
+  e = cudaFuncSetAttribute(ms::paged_attn_kernel<1, kTileWarps, kTileStages>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, TileCfg::kSmemBytes);
+  if (e != cudaSuccess) return cuda_fail("cudaFuncSetAttribute(tile)", e);
+  done[dev] = true;
+  return MS_OK;
+}
+
+static bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+static int check_pool(const void* k_cache, const void* v_cache, int num_blocks, int num_kv) {
+  if (k_cache == nullptr || v_cache == nullptr || num_blocks <= 0 || num_kv <= 0) {
+    set_error("KV pool: null pointer or empty pool");
+    return MS_ERR_ARG;
+  }
+  if (static_cast<const char*>(v_cache) != static_cast<const char*>(k_cache) + ms::kPageBytes) {
+    set_error("KV pool: v_cache must start 4096 bytes after k_cache (layout "
+              "[blocks][kv_heads][K,V][d/64][16][64])");
+    return MS_ERR_LAYOUT;
+  }
+  if (!aligned(k_cache, 16)) {
+    set_error("KV pool: k_cache must be 16-byte aligned");
+    return MS_ERR_LAYOUT;
+  }
+  return MS_OK;
+}
+
+}  // namespace ms_host
+
+using namespace ms_host;
+
+extern "C" int ms_version(void) { return MS_ABI_VERSION * 100 + 0; }
+
+extern "C" const char* ms_last_error(void) { return g_last_error.c_str(); }
+
+extern "C" int ms_device_status(void* stream, uint32_t* flags, int clear) {
+  if (flags == nullptr) {
+    set_error("ms_device_status: null flags");
+    return MS_ERR_ARG;
+  }
+  cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail("cudaStreamSynchronize", e);
+  unsigned v = 0;
+  e = cudaMemcpyFromSymbol(&v, ms::g_status_word, sizeof(v));
+  if (e != cudaSuccess) return cuda_fail("cudaMemcpyFromSymbol", e);
+  *flags = v;
+  if (clear) {
+    const unsigned zero = 0;
+    e = cudaMemcpyToSymbol(ms::g_status_word, &zero, sizeof(zero));
+    if (e != cudaSuccess) return cuda_fail("cudaMemcpyToSymbol", e);
+  }
+  return MS_OK;
+}
+
+static unsigned* status_ptr(int* rc) {
+  // Address of this device's status word (a __device__ symbol has one instance per device).
+  static thread_local int cached_dev = -1;
+  static thread_local unsigned* cached = nullptr;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    *rc = cuda_fail("cudaGetDevice", e);
+    return nullptr;
+  }
+  if (dev != cached_dev) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, ms::g_status_word);
+    if (e != cudaSuccess) {
+      *rc = cuda_fail("cudaGetSymbolAddress(status)", e);
+      return nullptr;
+    }
+    cached = static_cast<unsigned*>(p);
+    cached_dev = dev;
+  }
+  *rc = MS_OK;
+  return cached;
+}
+
+extern "C" int ms_qk_norm_rope_scatter(const void* qkv, int64_t qkv_row_stride, int32_t num_tokens,
+                                       int32_t num_heads, int32_t num_kv_heads,
+                                       const void* q_weight, const void* k_weight, float eps,
+                                       const float* cos, const float* sin, int64_t cs_row_stride,
+                                       const int64_t* positions, int64_t max_positions,
+                                       const int64_t* slot_mapping, void* q_out,
+                                       int64_t q_out_row_stride, void* k_cache, void* v_cache,
+                                       int32_t num_blocks, void* stream) {
+  if (num_tokens < 0 || num_kv_heads <= 0 || num_heads != ms::kGroup * num_kv_heads) {
+    set_error("ms_qk_norm_rope_scatter: need num_heads == 2 * num_kv_heads > 0, num_tokens >= 0");
+    return MS_ERR_ARG;
+  }
+  if (num_tokens == 0) return MS_OK;
+  int rc = check_pool(k_cache, v_cache, num_blocks, num_kv_heads);
+  if (rc) return rc;
+  if (!qkv || !q_weight || !k_weight || !cos || !sin || !slot_mapping || !q_out) {
+    set_error("ms_qk_norm_rope_scatter: null pointer argument");
+    return MS_ERR_ARG;
+  }
+  const int64_t width = static_cast<int64_t>(num_heads + 2 * num_kv_heads) * ms::kHeadDim;
+  if (qkv_row_stride < width || q_out_row_stride < num_heads * ms::kHeadDim ||
+      cs_row_stride < ms::kHeadDim || qkv_row_stride % 4 || q_out_row_stride % 4 ||
+      cs_row_stride % 4 || !aligned(qkv, 8) || !aligned(q_out, 8) || !aligned(cos, 16) ||
+      !aligned(sin, 16)) {
+    set_error("ms_qk_norm_rope_scatter: strides/alignment (qkv, q_out rows 8-byte aligned; "
+              "cos/sin rows 16-byte aligned)");
+    return MS_ERR_ARG;
+  }
+  if (positions != nullptr && max_positions <= 0) {
+    set_error("ms_qk_norm_rope_scatter: positions given with an empty table");
+    return MS_ERR_ARG;
+  }
+  unsigned* st = status_ptr(&rc);
+  if (rc) return rc;
+  ms::NormRopeArgs a;
+  a.qkv = static_cast<const __nv_bfloat16*>(qkv);
+  a.qkv_row_stride = qkv_row_stride;
+  a.q_weight = static_cast<const __nv_bfloat16*>(q_weight);
+  a.k_weight = static_cast<const __nv_bfloat16*>(k_weight);
+  a.eps = eps;
+  a.cos = cos;
+  a.sin = sin;
+  a.cs_row_stride = cs_row_stride;
+  a.positions = reinterpret_cast<const long long*>(positions);
+  a.max_positions = max_positions;
+  a.slots = reinterpret_cast<const long long*>(slot_mapping);
+  a.q_out = static_cast<__nv_bfloat16*>(q_out);
+  a.q_out_row_stride = q_out_row_stride;
+  a.k_pool = static_cast<__nv_bfloat16*>(k_cache);
+  a.head_stride = ms::kPageKVBytes / 2;
+  a.block_stride = static_cast<long long>(num_kv_heads) * a.head_stride;
+  a.num_slots = static_cast<long long>(num_blocks) * ms::kBlockTokens;
+  a.num_tokens = num_tokens;
+  a.num_heads = num_heads;
+  a.num_kv = num_kv_heads;
+  constexpr int kWarps = 8;
+  const long long warps = static_cast<long long>(num_tokens) * (num_heads + 2 * num_kv_heads);
+  const long long blocks = (warps + kWarps - 1) / kWarps;
+  if (blocks > 0x7fffffffLL) {
+    set_error("ms_qk_norm_rope_scatter: batch too large");
+    return MS_ERR_ARG;
+  }
+  ms::qk_norm_rope_scatter_kernel<kWarps>
+      <<<static_cast<unsigned>(blocks), kWarps * 32, 0, static_cast<cudaStream_t>(stream)>>>(a, st);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail("qk_norm_rope_scatter launch", e);
+  return MS_OK;
+}
+
+extern "C" int ms_kv_scatter(const void* k, int64_t k_row_stride, const void* v,
+                             int64_t v_row_stride, int32_t num_tokens, int32_t num_kv_heads,
+                             const int64_t* slot_mapping, void* k_cache, void* v_cache,
+                             int32_t num_blocks, void* stream) {
+  if (num_tokens < 0 || num_kv_heads <= 0) {
+    set_error("ms_kv_scatter: bad sizes");
+    return MS_ERR_ARG;
+  }
+  if (num_tokens == 0) return MS_OK;
+  int rc = check_pool(k_cache, v_cache, num_blocks, num_kv_heads);
+  if (rc) return rc;
+  if (!k || !v || !slot_mapping || k_row_stride < num_kv_heads * ms::kHeadDim ||
+      v_row_stride < num_kv_heads * ms::kHeadDim || k_row_stride % 4 || v_row_stride % 4 ||
+      !aligned(k, 8) || !aligned(v, 8)) {
+    set_error("ms_kv_scatter: null pointer, stride or alignment");
+    return MS_ERR_ARG;
+  }
+  unsigned* st = status_ptr(&rc);
+  if (rc) return rc;
+  ms::ScatterArgs a;
+  a.k = static_cast<const __nv_bfloat16*>(k);
+  a.k_row_stride = k_row_stride;
+  a.v = static_cast<const __nv_bfloat16*>(v);
+  a.v_row_stride = v_row_stride;
+  a.slots = reinterpret_cast<const long long*>(slot_mapping);
+  a.k_pool = static_cast<__nv_bfloat16*>(k_cache);
+  a.head_stride = ms::kPageKVBytes / 2;
+  a.block_stride = static_cast<long long>(num_kv_heads) * a.head_stride;
+  a.num_slots = static_cast<long long>(num_blocks) * ms::kBlockTokens;
+  a.num_tokens = num_tokens;
+  a.num_kv = num_kv_heads;
+  constexpr int kWarps = 8;
+  const long long warps = static_cast<long long>(num_tokens) * 2 * num_kv_heads;
+  const long long blocks = (warps + kWarps - 1) / kWarps;
+  ms::kv_scatter_kernel<kWarps>
+      <<<static_cast<unsigned>(blocks), kWarps * 32, 0, static_cast<cudaStream_t>(stream)>>>(a, st);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail("kv_scatter launch", e);
+  return MS_OK;
+}
+
+extern "C" int ms_paged_attention(const void* q, int64_t q_row_stride, void* out,
+                                  int64_t out_row_stride, int32_t num_heads, int32_t num_kv_heads,
+                                  const void* k_cache, const void* v_cache, int32_t num_blocks,
+                                  const int32_t* plan_dev, const MsPlanInfo* plan, void* workspace,
+                                  int64_t workspace_bytes, float scale, void* stream) {
+  if (plan == nullptr || num_kv_heads <= 0 || num_heads != ms::kGroup * num_kv_heads) {
+    set_error("ms_paged_attention: need a plan and num_heads == 2 * num_kv_heads > 0");
+    return MS_ERR_ARG;
+  }
+  const int64_t n_items = static_cast<int64_t>(plan->n_decode_items) + plan->n_tile_items;
+  if (n_items == 0) return MS_OK;
+  int rc = check_pool(k_cache, v_cache, num_blocks, num_kv_heads);
+  if (rc) return rc;
+  if (!q || !out || !plan_dev || q_row_stride < num_heads * ms::kHeadDim ||
+      out_row_stride < num_heads * ms::kHeadDim || q_row_stride % 8 || out_row_stride % 8 ||
+      !aligned(q, 16) || !aligned(out, 16) || !aligned(plan_dev, 16)) {
+    set_error("ms_paged_attention: null pointer, or q/out rows not 16-byte aligned");
+    return MS_ERR_ARG;
+  }
+  const int64_t need = plan->workspace_bytes_per_kv_head * num_kv_heads;
+  if (need > 0 && (workspace == nullptr || workspace_bytes < need || !aligned(workspace, 16))) {
+    set_error("ms_paged_attention: workspace of " + std::to_string(need) +
+              " bytes (16-byte aligned) required");
+    return MS_ERR_ARG;
+  }
+  if (n_items * num_kv_heads > 0x7fffffffLL ||
+      static_cast<int64_t>(plan->n_combine) * num_kv_heads > 0x7fffffffLL) {
+    set_error("ms_paged_attention: plan too large for one launch");
+    return MS_ERR_ARG;
+  }
+  rc = ensure_smem_attrs();
+  if (rc) return rc;
+  CUtensorMap map;
+  rc = kv_tensor_map(k_cache, num_blocks, num_kv_heads, &map);
+  if (rc) return rc;
+
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  ms::AttnArgs a;
+  a.q = static_cast<const __nv_bfloat16*>(q);
+  a.q_row_stride = q_row_stride;
+  a.out = static_cast<__nv_bfloat16*>(out);
+  a.out_row_stride = out_row_stride;
+  a.seqs = plan_dev + plan->off_seqs;
+  a.tables = plan_dev + plan->off_tables;
+  a.num_kv = num_kv_heads;
+  a.num_blocks = num_blocks;
+  float* ws = static_cast<float*>(workspace);
+  a.ws_o = ws;
+  a.ws_lse = ws != nullptr ? ws + plan->part_rows * num_kv_heads * ms::kHeadDim : nullptr;
+  a.scale_log2 = scale * 1.4426950408889634f;
+
+  if (plan->n_decode_items > 0) {
+    a.items = plan_dev + plan->off_decode;
+    a.n_items = plan->n_decode_items;
+    ms::paged_attn_kernel<0, kDecodeWarps, kDecodeStages>
+        <<<plan->n_decode_items * num_kv_heads, DecodeCfg::kThreads, DecodeCfg::kSmemBytes, s>>>(map, a);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail("paged_attn decode launch", e);
+  }
+  if (plan->n_tile_items > 0) {
+    a.items = plan_dev + plan->off_tile;
+    a.n_items = plan->n_tile_items;
+    ms::paged_attn_kernel<1, kTileWarps, kTileStages>
+        <<<plan->n_tile_items * num_kv_heads, TileCfg::kThreads, TileCfg::kSmemBytes, s>>>(map, a);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail("paged_attn tile launch", e);
+  }
+  if (plan->n_combine > 0) {
+    ms::CombineArgs c;
+    c.out = a.out;
+    c.out_row_stride = out_row_stride;
+    c.seqs = a.seqs;
+    c.combines = plan_dev + plan->off_combine;
+    c.n_combine = plan->n_combine;
+    c.num_kv = num_kv_heads;
+    c.ws_o = a.ws_o;
+    c.ws_lse = a.ws_lse;
+    ms::combine_kernel<<<plan->n_combine * num_kv_heads, 128, 0, s>>>(c);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail("combine launch", e);
+  }
+  return MS_OK;
+}

@@ -1,0 +1,183 @@
+// Kernel A: fused per-head q/k RMSNorm + rotate-half RoPE + scatter of the new K/V rows into the
+// paged KV pool.  Replaces, for one layer, the op sequence of MiniServe's attention module
+// (src/miniserve/model/qwen3.py:94-98 -> layers.py:18-22 and :56-65) and the scatter at the top of
+// paged_attention (src/miniserve/attention/backends.py:159-160).
+//
+// One warp handles one (token, head row) pair: rows 0..H-1 are query heads, H..H+KVH-1 key heads,
+// H+KVH..H+2*KVH-1 value heads, i.e. the 128-column blocks of the fused qkv projection in order.
+// Each lane owns 4 consecutive dims (one 8-byte load, one 8-byte store).
+//
+// Rounding follows the reference exactly where the order is fixed by it: fp32 squares, fp32 mean,
+// rsqrt, fp32 multiply, round to bf16, bf16 weight multiply (rounded), bf16 cos/sin, bf16 products
+// and a bf16 sum.  __fmul_rn/__fadd_rn keep nvcc from contracting these into FMAs.  Only the
+// summation order of the 128 squares differs from PyTorch's reduction kernel, which can move the
+// fp32 mean by an ulp and, rarely, one output by one bf16 ulp.
+#pragma once
+
+#include "ms_common.cuh"
+
+namespace ms {
+
+struct NormRopeArgs {
+  const __nv_bfloat16* qkv;  // [T, (H + 2*KVH) * 128]
+  long long qkv_row_stride;  // elements
+  const __nv_bfloat16* q_weight;  // [128]
+  const __nv_bfloat16* k_weight;  // [128]
+  float eps;
+  const float* cos;  // [T, 128] rows already gathered by position, or the [max_pos, 128] table
+  const float* sin;
+  long long cs_row_stride;
+  const long long* positions;  // null: cos/sin are per-token rows; else index into the table
+  long long max_positions;
+  const long long* slots;  // [T] slot = block * 16 + offset
+  __nv_bfloat16* q_out;  // [T, H, 128]
+  long long q_out_row_stride;
+  __nv_bfloat16* k_pool;  // this layer's K base; V base = K base + 2048 elements
+  long long block_stride;  // elements between blocks
+  long long head_stride;   // elements between KV heads of one block
+  long long num_slots;
+  int num_tokens;
+  int num_heads;
+  int num_kv;
+};
+
+// Element offset of (slot, kv head, dim) inside a layer's K region of the pool.
+// Within a (block, head) the K page is [d/64][token][d%64]; V follows 4 KiB later.
+__device__ __forceinline__ long long pool_offset(long long slot, int head, int d,
+                                                 long long block_stride, long long head_stride) {
+  const long long block = slot >> 4;
+  const int tok = static_cast<int>(slot & 15);
+  return block * block_stride + head * head_stride + (d >> 6) * (kBlockTokens * 64) + tok * 64 +
+         (d & 63);
+}
+
+__device__ __forceinline__ float bf16_round(float x) {
+  return __bfloat162float(__float2bfloat16_rn(x));
+}
+
+template <int kWarps>
+__global__ void __launch_bounds__(kWarps * 32)
+    qk_norm_rope_scatter_kernel(const NormRopeArgs a, unsigned* status) {
+  const int lane = threadIdx.x & 31;
+  const long long gw = static_cast<long long>(blockIdx.x) * kWarps + (threadIdx.x >> 5);
+  const int rows_per_tok = a.num_heads + 2 * a.num_kv;
+  const long long t = gw / rows_per_tok;
+  if (t >= a.num_tokens) return;
+  const int hr = static_cast<int>(gw - t * rows_per_tok);
+  const int d0 = lane * 4;
+
+  const uint2 raw =
+      *reinterpret_cast<const uint2*>(a.qkv + t * a.qkv_row_stride + hr * kHeadDim + d0);
+
+  if (hr >= a.num_heads + a.num_kv) {  // value head: a pure copy into the pool
+    const long long slot = a.slots[t];
+    if (slot < 0 || slot >= a.num_slots) {
+      if (lane == 0) atomicOr(status, kErrSlot);
+      return;
+    }
+    const int h = hr - a.num_heads - a.num_kv;
+    __nv_bfloat16* dst =
+        a.k_pool + 2 * kBlockTokens * 64 + pool_offset(slot, h, d0, a.block_stride, a.head_stride);
+    *reinterpret_cast<uint2*>(dst) = raw;
+    return;
+  }
+
+  const bool is_q = hr < a.num_heads;
+  const __nv_bfloat16* xb = reinterpret_cast<const __nv_bfloat16*>(&raw);
+  float x[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) x[i] = __bfloat162float(xb[i]);
+
+  // fp32 mean of squares over the 128 dims of this head.
+  float ss = __fadd_rn(__fadd_rn(__fmul_rn(x[0], x[0]), __fmul_rn(x[1], x[1])),
+                       __fadd_rn(__fmul_rn(x[2], x[2]), __fmul_rn(x[3], x[3])));
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, off));
+  const float inv = rsqrtf(__fadd_rn(__fmul_rn(ss, 1.0f / kHeadDim), a.eps));
+
+  const __nv_bfloat16* w = (is_q ? a.q_weight : a.k_weight) + d0;
+  float z[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float y = bf16_round(__fmul_rn(x[i], inv));            // (x32 * rsqrt).to(bf16)
+    z[i] = bf16_round(__fmul_rn(__bfloat162float(w[i]), y));     // weight * y, in bf16
+  }
+
+  // RoPE: dim d pairs with d +/- 64, i.e. lane +/- 16.
+  long long pos_row = t;
+  if (a.positions != nullptr) {
+    pos_row = a.positions[t];
+    if (pos_row < 0 || pos_row >= a.max_positions) {
+      if (lane == 0) atomicOr(status, kErrPosition);
+      pos_row = 0;
+    }
+  }
+  const float4 c4 = *reinterpret_cast<const float4*>(a.cos + pos_row * a.cs_row_stride + d0);
+  const float4 s4 = *reinterpret_cast<const float4*>(a.sin + pos_row * a.cs_row_stride + d0);
+  const float cv[4] = {bf16_round(c4.x), bf16_round(c4.y), bf16_round(c4.z), bf16_round(c4.w)};
+  const float sv[4] = {bf16_round(s4.x), bf16_round(s4.y), bf16_round(s4.z), bf16_round(s4.w)};
+
+  __nv_bfloat16 outv[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float partner = __shfl_xor_sync(0xffffffffu, z[i], 16);
+    const float rot = lane < 16 ? -partner : partner;  // rotate_half: [-x2, x1]
+    const float p1 = bf16_round(__fmul_rn(z[i], cv[i]));
+    const float p2 = bf16_round(__fmul_rn(rot, sv[i]));
+    outv[i] = __float2bfloat16_rn(__fadd_rn(p1, p2));
+  }
+  const uint2 packed = *reinterpret_cast<const uint2*>(outv);
+
+  if (is_q) {
+    *reinterpret_cast<uint2*>(a.q_out + t * a.q_out_row_stride + hr * kHeadDim + d0) = packed;
+    return;
+  }
+  const long long slot = a.slots[t];
+  if (slot < 0 || slot >= a.num_slots) {
+    if (lane == 0) atomicOr(status, kErrSlot);
+    return;
+  }
+  __nv_bfloat16* dst =
+      a.k_pool + pool_offset(slot, hr - a.num_heads, d0, a.block_stride, a.head_stride);
+  *reinterpret_cast<uint2*>(dst) = packed;
+}
+
+struct ScatterArgs {
+  const __nv_bfloat16* k;  // [T, KVH, 128] (row stride k_row_stride, head stride 128)
+  long long k_row_stride;
+  const __nv_bfloat16* v;
+  long long v_row_stride;
+  const long long* slots;
+  __nv_bfloat16* k_pool;
+  long long block_stride;
+  long long head_stride;
+  long long num_slots;
+  int num_tokens;
+  int num_kv;
+};
+
+// Scatter-only form (backends.py:159-160 alone): k and v are already normalised/rotated.
+template <int kWarps>
+__global__ void __launch_bounds__(kWarps * 32) kv_scatter_kernel(const ScatterArgs a,
+                                                                 unsigned* status) {
+  const int lane = threadIdx.x & 31;
+  const long long gw = static_cast<long long>(blockIdx.x) * kWarps + (threadIdx.x >> 5);
+  const long long t = gw / (2 * a.num_kv);
+  if (t >= a.num_tokens) return;
+  const int r = static_cast<int>(gw - t * 2 * a.num_kv);
+  const bool is_v = r >= a.num_kv;
+  const int h = is_v ? r - a.num_kv : r;
+  const int d0 = lane * 4;
+  const long long slot = a.slots[t];
+  if (slot < 0 || slot >= a.num_slots) {
+    if (lane == 0) atomicOr(status, kErrSlot);
+    return;
+  }
+  const __nv_bfloat16* src =
+      is_v ? a.v + t * a.v_row_stride + h * kHeadDim + d0 : a.k + t * a.k_row_stride + h * kHeadDim + d0;
+  __nv_bfloat16* dst = a.k_pool + (is_v ? 2 * kBlockTokens * 64 : 0) +
+                       pool_offset(slot, h, d0, a.block_stride, a.head_stride);
+  *reinterpret_cast<uint2*>(dst) = *reinterpret_cast<const uint2*>(src);
+}
+
+}  // namespace ms

@@ -1,0 +1,462 @@
+// Kernel B: paged attention over the KV pool, read in place through the block tables.
+// Kernel C: merge of split-KV partial results.
+//
+// Replaces the gather + SDPA loops of MiniServe's paged_attention
+// (src/miniserve/attention/backends.py:165-196).  One CTA owns one work item for one KV head: a
+// tile of query tokens of one sequence (both query heads of the GQA pair folded into the rows,
+// row = token * 2 + head-in-pair) and a contiguous range of that sequence's KV pages.
+//
+//   * A producer warp walks the block table and issues one 8 KiB TMA tensor load per page
+//     (K and V of this head, 128-byte swizzled, no multicast) into a ring of shared-memory
+//     stages guarded by full/empty mbarriers.
+//   * Consumer warps compute S = Q K^T and O += P V with mma.sync m16n8k16 (bf16 in, fp32
+//     accumulate) and an fp32 online softmax in the exp2 domain.
+//   * Decode mode (<= 8 query tokens, 16 rows): each consumer warp takes every 4th page and the
+//     warps merge their (m, l, O) in shared memory at the end.
+//   * Tile mode (up to 64 query tokens, 128 rows): each consumer warp owns 16 rows and reads
+//     every page; causal masking uses the sequence's cached length as the offset.
+//   * An item that covers the whole visible context writes bf16 output rows directly; a split
+//     item writes normalised fp32 partials + log2-sum-exp, merged by kernel C.
+//
+// The masking rule is the reference's: the query at position num_cached + i sees keys
+// 0..num_cached + i (backends.py:123-125, :140-142).
+#pragma once
+
+#include "ms_common.cuh"
+
+namespace ms {
+
+// Packed plan records (int32 x 8 each); the host planner writes them.
+//   sequence: {flat_start, num_new, num_cached, context_len, table_offset, table_len, 0, 0}
+//   item:     {seq, tok0, n_q, page_begin, page_end, part_row (-1 = write output), 0, 0}
+//   combine:  {seq, tok0, n_q, part_row0, n_splits, 0, 0, 0}
+constexpr int kRec = 8;
+
+struct AttnArgs {
+  const __nv_bfloat16* q;  // [T, H, 128]
+  long long q_row_stride;
+  __nv_bfloat16* out;  // [T, H, 128]
+  long long out_row_stride;
+  const int* seqs;    // sequence records
+  const int* tables;  // flat block tables
+  const int* items;   // this launch's items
+  int n_items;
+  int num_kv;
+  int num_blocks;
+  float* ws_o;    // [part_rows, KVH, 128] fp32 partials
+  float* ws_lse;  // [part_rows, KVH]
+  float scale_log2;
+};
+
+template <int kMode, int kConsumerWarps, int kStages>
+struct AttnCfg {
+  static constexpr int kRows = kMode == 0 ? 16 : 16 * kConsumerWarps;
+  static constexpr int kThreads = (kConsumerWarps + 1) * 32;
+  static constexpr int kStageBytes = kStages * kPageKVBytes;
+  static constexpr int kQBytes = kRows * kHeadDim * 2;
+  static constexpr int kMergeBytes = kMode == 0 ? kConsumerWarps * 16 * (kHeadDim + 4) * 4 + 2 * kConsumerWarps * 16 * 4 : 0;
+  static_assert(kMergeBytes <= kStageBytes, "merge scratch reuses the stage ring");
+  static constexpr int kBarOffset = kStageBytes + kQBytes;
+  static constexpr int kSmemBytes = 1024 + kBarOffset + 2 * kStages * 8 + 16;
+};
+
+// One 16-key page for one warp's 16 query rows.
+__device__ __forceinline__ void attend_page(uint32_t stage, const uint32_t (&qf)[8][4],
+                                            float (&o)[16][4], float (&m)[2], float (&l)[2],
+                                            int key0, int qpos0, int qpos1, bool need_mask,
+                                            float scale_log2, int lane) {
+  float s0[4] = {0.f, 0.f, 0.f, 0.f};
+  float s1[4] = {0.f, 0.f, 0.f, 0.f};
+  const int mi = lane >> 3;
+  {
+    const int key = (lane & 7) + (mi >> 1) * 8;
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+      uint32_t b0, b1, b2, b3;
+      ldsm_x4(stage + swz_off(key, ks * 16 + (mi & 1) * 8, 16), b0, b1, b2, b3);
+      mma_bf16(s0, qf[ks], b0, b1);
+      mma_bf16(s1, qf[ks], b2, b3);
+    }
+  }
+  const float ninf = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    s0[i] *= scale_log2;
+    s1[i] *= scale_log2;
+  }
+  if (need_mask) {
+    const int ka = key0 + 2 * (lane & 3);
+    const int kb = ka + 8;
+    if (ka > qpos0) s0[0] = ninf;
+    if (ka + 1 > qpos0) s0[1] = ninf;
+    if (ka > qpos1) s0[2] = ninf;
+    if (ka + 1 > qpos1) s0[3] = ninf;
+    if (kb > qpos0) s1[0] = ninf;
+    if (kb + 1 > qpos0) s1[1] = ninf;
+    if (kb > qpos1) s1[2] = ninf;
+    if (kb + 1 > qpos1) s1[3] = ninf;
+  }
+  float mx0 = fmaxf(fmaxf(s0[0], s0[1]), fmaxf(s1[0], s1[1]));
+  float mx1 = fmaxf(fmaxf(s0[2], s0[3]), fmaxf(s1[2], s1[3]));
+  mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+  mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+  mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+  mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+  const float mn0 = fmaxf(m[0], mx0);
+  const float mn1 = fmaxf(m[1], mx1);
+  const float mu0 = mn0 == ninf ? 0.f : mn0;
+  const float mu1 = mn1 == ninf ? 0.f : mn1;
+  const float al0 = fast_exp2(m[0] - mu0);
+  const float al1 = fast_exp2(m[1] - mu1);
+  m[0] = mn0;
+  m[1] = mn1;
+  float p0[4], p1[4];
+  p0[0] = fast_exp2(s0[0] - mu0);
+  p0[1] = fast_exp2(s0[1] - mu0);
+  p0[2] = fast_exp2(s0[2] - mu1);
+  p0[3] = fast_exp2(s0[3] - mu1);
+  p1[0] = fast_exp2(s1[0] - mu0);
+  p1[1] = fast_exp2(s1[1] - mu0);
+  p1[2] = fast_exp2(s1[2] - mu1);
+  p1[3] = fast_exp2(s1[3] - mu1);
+  l[0] = l[0] * al0 + ((p0[0] + p0[1]) + (p1[0] + p1[1]));
+  l[1] = l[1] * al1 + ((p0[2] + p0[3]) + (p1[2] + p1[3]));
+#pragma unroll
+  for (int n = 0; n < 16; ++n) {
+    o[n][0] *= al0;
+    o[n][1] *= al0;
+    o[n][2] *= al1;
+    o[n][3] *= al1;
+  }
+  const uint32_t pa[4] = {pack_bf16(p0[0], p0[1]), pack_bf16(p0[2], p0[3]),
+                          pack_bf16(p1[0], p1[1]), pack_bf16(p1[2], p1[3])};
+  {
+    const int key = (lane & 7) + (mi & 1) * 8;
+    const uint32_t vbase = stage + kPageBytes;
+#pragma unroll
+    for (int np = 0; np < 8; ++np) {
+      uint32_t b0, b1, b2, b3;
+      ldsm_x4_t(vbase + swz_off(key, np * 16 + (mi >> 1) * 8, 16), b0, b1, b2, b3);
+      mma_bf16(o[2 * np], pa, b0, b1);
+      mma_bf16(o[2 * np + 1], pa, b2, b3);
+    }
+  }
+}
+
+__device__ unsigned g_status_word;  // device status bits (kErr*), read by ms_device_status
+
+template <int kMode, int kConsumerWarps, int kStages>
+__global__ void __launch_bounds__(AttnCfg<kMode, kConsumerWarps, kStages>::kThreads)
+    paged_attn_kernel(const __grid_constant__ CUtensorMap kv_map, const AttnArgs a) {
+  using Cfg = AttnCfg<kMode, kConsumerWarps, kStages>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* ring = smem;
+  uint8_t* qtile = smem + Cfg::kStageBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::kBarOffset);
+  uint64_t* empty = full + kStages;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kStages);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int item_idx = blockIdx.x / a.num_kv;
+  const int kvh = blockIdx.x - item_idx * a.num_kv;
+  const int* it = a.items + static_cast<long long>(item_idx) * kRec;
+  const int seq = it[0], tok0 = it[1], n_q = it[2], page_begin = it[3], page_end = it[4],
+            part_row = it[5];
+  const int* sr = a.seqs + static_cast<long long>(seq) * kRec;
+  const int flat_start = sr[0], num_cached = sr[2], table_off = sr[4];
+  const int npages = page_end - page_begin;
+
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kMode == 0 ? 1 : kConsumerWarps);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+
+  // Query tile -> shared memory, swizzled like a page: [16-row group][d/64][row][d%64].
+  if (warp < kConsumerWarps) {
+    const int nthreads = kConsumerWarps * 32;
+    for (int c = threadIdx.x; c < Cfg::kRows * 16; c += nthreads) {
+      const int r = c >> 4;
+      const int d = (c & 15) * 8;
+      const int tok = r >> 1;
+      uint4 v = make_uint4(0u, 0u, 0u, 0u);
+      if (tok < n_q) {
+        const __nv_bfloat16* src = a.q + static_cast<long long>(flat_start + tok0 + tok) * a.q_row_stride +
+                                   (kvh * kGroup + (r & 1)) * kHeadDim + d;
+        v = *reinterpret_cast<const uint4*>(src);
+      }
+      *reinterpret_cast<uint4*>(qtile + (r >> 4) * (16 * kHeadDim * 2) + swz_off(r & 15, d, 16)) = v;
+    }
+  }
+  __syncthreads();
+
+  if (warp == kConsumerWarps) {
+    // ---------------- producer warp ----------------
+    const uint64_t policy = l2_policy_evict_first();
+    if (lane == 0) tma_prefetch_desc(&kv_map);
+    const int* table = a.tables + table_off + page_begin;
+    int issued = 0;
+    bool stop = false;
+    for (int j0 = 0; j0 < npages && !stop; j0 += 32) {
+      int mine = 0;
+      if (j0 + lane < npages) mine = table[j0 + lane];
+      const int cnt = min(32, npages - j0);
+      for (int jj = 0; jj < cnt; ++jj) {
+        const int blk = __shfl_sync(0xffffffffu, mine, jj);
+        int ok = 1;
+        if (lane == 0) {
+          const int j = j0 + jj;
+          const int s = j % kStages;
+          if (*abort_flag) ok = 0;
+          if (ok && j >= kStages && !mbar_wait(&empty[s], ((j / kStages) - 1) & 1)) {
+            atomicOr(&g_status_word, kErrTimeout);
+            *abort_flag = 1;
+            ok = 0;
+          }
+          if (ok) {
+            // Out-of-range block ids are flagged; the TMA unit fills such boxes with zeros.
+            if (static_cast<unsigned>(blk) >= static_cast<unsigned>(a.num_blocks))
+              atomicOr(&g_status_word, kErrBlock);
+            mbar_arrive_expect_tx(&full[s], kPageKVBytes);
+            tma_load_5d(ring + s * kPageKVBytes, &kv_map, &full[s], 0, 0, 0, kvh, blk, policy);
+            ++issued;
+          }
+        }
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) {
+          stop = true;
+          break;
+        }
+      }
+    }
+    // Drain: never leave the CTA with a TMA write in flight.
+    if (lane == 0) {
+      const int first = issued > kStages ? issued - kStages : 0;
+      for (int j = first; j < issued; ++j) {
+        if (!mbar_wait(&full[j % kStages], (j / kStages) & 1)) {
+          atomicOr(&g_status_word, kErrTimeout);
+          break;
+        }
+      }
+    }
+    return;
+  }
+
+  // ---------------- consumer warps ----------------
+  const int row_base = kMode == 0 ? 0 : warp * 16;
+  uint32_t qf[8][4];
+  {
+    const uint32_t qbase = smem_u32(qtile) + (row_base >> 4) * (16 * kHeadDim * 2);
+    const int mi = lane >> 3;
+    const int row = (lane & 7) + (mi & 1) * 8;
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks)
+      ldsm_x4(qbase + swz_off(row, ks * 16 + (mi >> 1) * 8, 16), qf[ks][0], qf[ks][1], qf[ks][2],
+              qf[ks][3]);
+  }
+  float o[16][4];
+#pragma unroll
+  for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+  float m[2] = {-INFINITY, -INFINITY};
+  float l[2] = {0.f, 0.f};
+  const int r0 = row_base + (lane >> 2);
+  const int r1 = r0 + 8;
+  const int qpos_base = num_cached + tok0;
+  const int qpos0 = qpos_base + (r0 >> 1);
+  const int qpos1 = qpos_base + (r1 >> 1);
+  const int min_qpos = qpos_base + (row_base >> 1);         // first row of this warp's rows
+  const int max_qpos = qpos_base + ((row_base + 15) >> 1);  // last row (warp-uniform)
+  const uint32_t ring_u32 = smem_u32(ring);
+
+  const int jstart = kMode == 0 ? warp : 0;
+  const int jstep = kMode == 0 ? kConsumerWarps : 1;
+  const bool warp_active = kMode == 0 || (row_base >> 1) < n_q;
+  for (int j = jstart; j < npages; j += jstep) {
+    const int s = j % kStages;
+    // Leave the loop only as a whole warp: the tensor-core ops below are warp-collective.
+    const bool ok = __all_sync(0xffffffffu, *abort_flag == 0 && mbar_wait(&full[s], (j / kStages) & 1));
+    if (!ok) {
+      if (lane == 0) {
+        atomicOr(&g_status_word, kErrTimeout);
+        *abort_flag = 1;
+      }
+      break;
+    }
+    const int key0 = (page_begin + j) * kBlockTokens;
+    if (warp_active && key0 <= max_qpos) {
+      attend_page(ring_u32 + s * kPageKVBytes, qf, o, m, l, key0, qpos0, qpos1,
+                  key0 + kBlockTokens - 1 > min_qpos, a.scale_log2, lane);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+  }
+
+  // Row sums were kept per thread; finish them across the quad.
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    l[i] += __shfl_xor_sync(0xffffffffu, l[i], 1);
+    l[i] += __shfl_xor_sync(0xffffffffu, l[i], 2);
+  }
+
+  if constexpr (kMode == 0) {
+    // Cross-warp merge of the per-warp page subsets, through the (now idle) stage ring.
+    float* mo = reinterpret_cast<float*>(ring);
+    float* mm = mo + kConsumerWarps * 16 * (kHeadDim + 4);
+    float* ml = mm + kConsumerWarps * 16;
+    asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
+    {
+      float* wo = mo + warp * 16 * (kHeadDim + 4);
+      const int ra = lane >> 2, rb = ra + 8, c = 2 * (lane & 3);
+#pragma unroll
+      for (int n = 0; n < 16; ++n) {
+        *reinterpret_cast<float2*>(wo + ra * (kHeadDim + 4) + n * 8 + c) = make_float2(o[n][0], o[n][1]);
+        *reinterpret_cast<float2*>(wo + rb * (kHeadDim + 4) + n * 8 + c) = make_float2(o[n][2], o[n][3]);
+      }
+      if ((lane & 3) == 0) {
+        mm[warp * 16 + ra] = m[0];
+        mm[warp * 16 + rb] = m[1];
+        ml[warp * 16 + ra] = l[0];
+        ml[warp * 16 + rb] = l[1];
+      }
+    }
+    asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
+    const int tid = threadIdx.x;
+    for (int e = tid; e < 16 * 8; e += kConsumerWarps * 32) {
+      const int r = e >> 3;
+      const int dc = (e & 7) * 16;
+      const int tok = r >> 1;
+      if (tok >= n_q) continue;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int w = 0; w < kConsumerWarps; ++w) mx = fmaxf(mx, mm[w * 16 + r]);
+      float wsc[kConsumerWarps];
+      float L = 0.f;
+#pragma unroll
+      for (int w = 0; w < kConsumerWarps; ++w) {
+        const float mw = mm[w * 16 + r];
+        wsc[w] = mw == -INFINITY ? 0.f : fast_exp2(mw - mx);
+        L += ml[w * 16 + r] * wsc[w];
+      }
+      const float invL = L > 0.f ? 1.f / L : 0.f;
+      float acc[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) acc[i] = 0.f;
+#pragma unroll
+      for (int w = 0; w < kConsumerWarps; ++w) {
+        const float* src = mo + (w * 16 + r) * (kHeadDim + 4) + dc;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) acc[i] += src[i] * wsc[w];
+      }
+      const int head = kvh * kGroup + (r & 1);
+      if (part_row < 0) {
+        __nv_bfloat16* dst = a.out + static_cast<long long>(flat_start + tok0 + tok) * a.out_row_stride +
+                             head * kHeadDim + dc;
+        uint32_t pk[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) pk[i] = pack_bf16(acc[2 * i] * invL, acc[2 * i + 1] * invL);
+        reinterpret_cast<uint4*>(dst)[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        reinterpret_cast<uint4*>(dst)[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+      } else {
+        const long long prow = static_cast<long long>(part_row + r) * a.num_kv + kvh;
+        float* dst = a.ws_o + prow * kHeadDim + dc;
+#pragma unroll
+        for (int i = 0; i < 16; i += 4)
+          *reinterpret_cast<float4*>(dst + i) =
+              make_float4(acc[i] * invL, acc[i + 1] * invL, acc[i + 2] * invL, acc[i + 3] * invL);
+        if (dc == 0) a.ws_lse[prow] = L > 0.f ? mx + __log2f(L) : -INFINITY;
+      }
+    }
+  } else {
+    if (!warp_active) return;
+    const int c = 2 * (lane & 3);
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const int r = half == 0 ? r0 : r1;
+      const int tok = r >> 1;
+      if (tok >= n_q) continue;
+      const float L = l[half];
+      const float invL = L > 0.f ? 1.f / L : 0.f;
+      const int head = kvh * kGroup + (r & 1);
+      if (part_row < 0) {
+        __nv_bfloat16* dst = a.out + static_cast<long long>(flat_start + tok0 + tok) * a.out_row_stride +
+                             head * kHeadDim + c;
+#pragma unroll
+        for (int n = 0; n < 16; ++n)
+          *reinterpret_cast<uint32_t*>(dst + n * 8) =
+              pack_bf16(o[n][2 * half] * invL, o[n][2 * half + 1] * invL);
+      } else {
+        const long long prow = static_cast<long long>(part_row + r) * a.num_kv + kvh;
+        float* dst = a.ws_o + prow * kHeadDim + c;
+#pragma unroll
+        for (int n = 0; n < 16; ++n)
+          *reinterpret_cast<float2*>(dst + n * 8) =
+              make_float2(o[n][2 * half] * invL, o[n][2 * half + 1] * invL);
+        if ((lane & 3) == 0) a.ws_lse[prow] = L > 0.f ? m[half] + __log2f(L) : -INFINITY;
+      }
+    }
+  }
+}
+
+struct CombineArgs {
+  __nv_bfloat16* out;
+  long long out_row_stride;
+  const int* seqs;
+  const int* combines;
+  int n_combine;
+  int num_kv;
+  const float* ws_o;
+  const float* ws_lse;
+};
+
+// Kernel C: out = sum_s 2^(lse_s - M) * O_s / sum_s 2^(lse_s - M) for every split tile.
+__global__ void __launch_bounds__(128) combine_kernel(const CombineArgs a) {
+  const int ci = blockIdx.x / a.num_kv;
+  const int kvh = blockIdx.x - ci * a.num_kv;
+  const int* cr = a.combines + static_cast<long long>(ci) * kRec;
+  const int seq = cr[0], tok0 = cr[1], n_q = cr[2], part_row0 = cr[3], n_splits = cr[4];
+  const int flat_start = a.seqs[static_cast<long long>(seq) * kRec];
+  const int rows = n_q * kGroup;
+  const int dc = (threadIdx.x & 7) * 16;
+  for (int r = threadIdx.x >> 3; r < rows; r += 16) {
+    float mx = -INFINITY;
+    for (int s = 0; s < n_splits; ++s)
+      mx = fmaxf(mx, a.ws_lse[static_cast<long long>(part_row0 + s * rows + r) * a.num_kv + kvh]);
+    float acc[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) acc[i] = 0.f;
+    float L = 0.f;
+    for (int s = 0; s < n_splits; ++s) {
+      const long long prow = static_cast<long long>(part_row0 + s * rows + r) * a.num_kv + kvh;
+      const float lse = a.ws_lse[prow];
+      const float w = lse == -INFINITY ? 0.f : fast_exp2(lse - mx);
+      L += w;
+      const float4* src = reinterpret_cast<const float4*>(a.ws_o + prow * kHeadDim + dc);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float4 v = src[i];
+        acc[4 * i] += w * v.x;
+        acc[4 * i + 1] += w * v.y;
+        acc[4 * i + 2] += w * v.z;
+        acc[4 * i + 3] += w * v.w;
+      }
+    }
+    const float invL = L > 0.f ? 1.f / L : 0.f;
+    const int head = kvh * kGroup + (r & 1);
+    __nv_bfloat16* dst = a.out + static_cast<long long>(flat_start + tok0 + (r >> 1)) * a.out_row_stride +
+                         head * kHeadDim + dc;
+    uint32_t pk[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) pk[i] = pack_bf16(acc[2 * i] * invL, acc[2 * i + 1] * invL);
+    reinterpret_cast<uint4*>(dst)[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+    reinterpret_cast<uint4*>(dst)[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+  }
+}
+
+}  // namespace ms

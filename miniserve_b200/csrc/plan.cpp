@@ -1,0 +1,215 @@
+// Host planner: turns the step's batch description into the packed int32 plan every layer reads.
+//
+// Replaces build_attention_metadata and its helpers (src/miniserve/attention/backends.py:80-142).
+// The reference sorts short-query rows by context length, pads them into groups under a gather
+// cap, and builds int64 index tensors and boolean masks per group; prefill chunks get their own
+// slot lists and shifted causal masks.  Here nothing is padded or gathered: each sequence keeps
+// its own block table (CSR), and the work is cut into (query tile, KV page range) items:
+//   * a sequence with <= 8 new tokens (decode, speculative verify) is one decode tile;
+//   * a longer chunk is cut into tiles of 64 query tokens;
+//   * a tile's visible pages, ceil((num_cached + tok0 + n_q) / 16), are split into near-equal
+//     ranges of at most `pages_per_split` pages; split tiles get partial rows in the workspace
+//     and a combine record.
+// Items are ordered longest first so the hardware block scheduler fills the tail with short ones.
+#include <algorithm>
+#include <cstdint>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "../../include/msattn.h"
+
+namespace ms_host {
+void set_error(const std::string& msg);
+}
+
+namespace {
+
+constexpr int kRec = 8;
+constexpr int kDecodeMaxTokens = 8;  // backends.py:32 SHORT_QUERY: the batched (short) path
+constexpr int kTileTokens = 64;      // query tokens per tile-mode work item (128 rows)
+constexpr int kItemsPerSm = 4;       // automatic split size aims at this many items per SM
+
+struct Item {
+  int seq, tok0, n_q, pb, pe, part_row;
+};
+
+int64_t round4(int64_t x) { return (x + 3) & ~int64_t(3); }
+
+}  // namespace
+
+extern "C" int64_t ms_plan_capacity(int32_t num_seqs, int32_t num_tokens,
+                                    int64_t total_table_entries) {
+  // Every item covers at least one page and every tile at least one query token, so the number
+  // of items is bounded by tiles * pages; a looser closed form is enough: one decode/tile item per
+  // 16 table entries plus one per tile, plus as many combine records.
+  const int64_t tiles = static_cast<int64_t>(num_seqs) + num_tokens / kTileTokens + 1;
+  const int64_t items = tiles + total_table_entries;
+  return round4(static_cast<int64_t>(num_seqs) * kRec) + round4(total_table_entries) +
+         2 * round4(items * kRec) + round4(tiles * kRec) + 16;
+}
+
+extern "C" int ms_plan_build(int32_t num_seqs, const int32_t* flat_start, const int32_t* num_new,
+                             const int32_t* num_cached, const int64_t* table_offsets,
+                             const int32_t* tables, int32_t num_tokens, int32_t block_size,
+                             int32_t num_sms, int32_t pages_per_split, int32_t* out,
+                             int64_t out_capacity, MsPlanInfo* info) {
+  if (info == nullptr || out == nullptr) {
+    ms_host::set_error("ms_plan_build: null output");
+    return MS_ERR_ARG;
+  }
+  std::memset(info, 0, sizeof(*info));
+  if (num_seqs < 0 || num_tokens < 0 || block_size != 16 || num_sms <= 0 || pages_per_split < 0) {
+    ms_host::set_error("ms_plan_build: bad sizes (block_size must be 16, num_sms > 0)");
+    return MS_ERR_ARG;
+  }
+  if (num_seqs > 0 && (flat_start == nullptr || num_new == nullptr || num_cached == nullptr ||
+                       table_offsets == nullptr)) {
+    ms_host::set_error("ms_plan_build: null batch arrays");
+    return MS_ERR_ARG;
+  }
+  const int64_t total_entries = num_seqs > 0 ? table_offsets[num_seqs] : 0;
+  if (total_entries > 0 && tables == nullptr) {
+    ms_host::set_error("ms_plan_build: null block tables");
+    return MS_ERR_ARG;
+  }
+  if (total_entries >= (int64_t(1) << 31)) {
+    ms_host::set_error("ms_plan_build: block tables exceed 2^31 entries");
+    return MS_ERR_ARG;
+  }
+
+  // Validate sequences and cut query tiles.
+  std::vector<Item> tiles;
+  tiles.reserve(num_seqs);
+  int64_t total_pages = 0;
+  for (int i = 0; i < num_seqs; ++i) {
+    const int64_t n = num_new[i], c = num_cached[i], f = flat_start[i];
+    const int64_t tlen = table_offsets[i + 1] - table_offsets[i];
+    if (n < 1 || c < 0 || f < 0 || f + n > num_tokens || tlen < 0) {
+      ms_host::set_error("ms_plan_build: sequence " + std::to_string(i) +
+                         " has an invalid flat_start/num_new/num_cached");
+      return MS_ERR_PLAN;
+    }
+    const int64_t ctx = c + n;
+    if (ctx >= (int64_t(1) << 30)) {
+      ms_host::set_error("ms_plan_build: context too long");
+      return MS_ERR_PLAN;
+    }
+    if (tlen * block_size < ctx) {
+      ms_host::set_error("ms_plan_build: sequence " + std::to_string(i) + " needs " +
+                         std::to_string((ctx + block_size - 1) / block_size) +
+                         " blocks but its table has " + std::to_string(tlen));
+      return MS_ERR_PLAN;
+    }
+    const int step = n <= kDecodeMaxTokens ? kDecodeMaxTokens : kTileTokens;
+    for (int64_t t0 = 0; t0 < n; t0 += step) {
+      const int nq = static_cast<int>(std::min<int64_t>(step, n - t0));
+      const int pages = static_cast<int>((c + t0 + nq + block_size - 1) / block_size);
+      tiles.push_back({i, static_cast<int>(t0), nq, 0, pages, -1});
+      total_pages += pages;
+    }
+  }
+
+  int split = pages_per_split;
+  if (split == 0) {
+    const int64_t target = static_cast<int64_t>(num_sms) * kItemsPerSm;
+    split = static_cast<int>(std::clamp<int64_t>((total_pages + target - 1) / std::max<int64_t>(target, 1), 8, 512));
+  }
+
+  std::vector<Item> dec, til, comb;
+  int64_t part_rows = 0;
+  for (const Item& t : tiles) {
+    const int pages = t.pe;
+    const int ns = (pages + split - 1) / split;
+    std::vector<Item>& dst = t.n_q <= kDecodeMaxTokens && num_new[t.seq] <= kDecodeMaxTokens ? dec : til;
+    if (ns <= 1) {
+      dst.push_back({t.seq, t.tok0, t.n_q, 0, pages, -1});
+      continue;
+    }
+    const int rows = 2 * t.n_q;
+    if (part_rows + static_cast<int64_t>(ns) * rows >= (int64_t(1) << 31)) {
+      ms_host::set_error("ms_plan_build: too many partial rows");
+      return MS_ERR_PLAN;
+    }
+    const int base = pages / ns, rem = pages % ns;
+    int pb = 0;
+    for (int s = 0; s < ns; ++s) {
+      const int len = base + (s < rem ? 1 : 0);
+      dst.push_back({t.seq, t.tok0, t.n_q, pb, pb + len,
+                     static_cast<int>(part_rows + static_cast<int64_t>(s) * rows)});
+      pb += len;
+    }
+    comb.push_back({t.seq, t.tok0, t.n_q, static_cast<int>(part_rows), ns, 0});
+    part_rows += static_cast<int64_t>(ns) * rows;
+  }
+  auto longest_first = [](const Item& x, const Item& y) { return (x.pe - x.pb) > (y.pe - y.pb); };
+  std::stable_sort(dec.begin(), dec.end(), longest_first);
+  std::stable_sort(til.begin(), til.end(), longest_first);
+
+  const int64_t off_seqs = 0;
+  const int64_t off_tables = round4(off_seqs + static_cast<int64_t>(num_seqs) * kRec);
+  const int64_t off_decode = round4(off_tables + total_entries);
+  const int64_t off_tile = round4(off_decode + static_cast<int64_t>(dec.size()) * kRec);
+  const int64_t off_combine = round4(off_tile + static_cast<int64_t>(til.size()) * kRec);
+  const int64_t total = round4(off_combine + static_cast<int64_t>(comb.size()) * kRec);
+  if (total > out_capacity) {
+    ms_host::set_error("ms_plan_build: output buffer holds " + std::to_string(out_capacity) +
+                       " ints, plan needs " + std::to_string(total));
+    return MS_ERR_CAPACITY;
+  }
+  if (total >= (int64_t(1) << 31)) {
+    ms_host::set_error("ms_plan_build: plan larger than 2^31 ints");
+    return MS_ERR_PLAN;
+  }
+  std::memset(out, 0, sizeof(int32_t) * total);
+  for (int i = 0; i < num_seqs; ++i) {
+    int32_t* r = out + off_seqs + static_cast<int64_t>(i) * kRec;
+    r[0] = flat_start[i];
+    r[1] = num_new[i];
+    r[2] = num_cached[i];
+    r[3] = num_cached[i] + num_new[i];
+    r[4] = static_cast<int32_t>(table_offsets[i]);
+    r[5] = static_cast<int32_t>(table_offsets[i + 1] - table_offsets[i]);
+  }
+  if (total_entries > 0) std::memcpy(out + off_tables, tables, sizeof(int32_t) * total_entries);
+  auto put = [&](int64_t off, const std::vector<Item>& v) {
+    for (size_t k = 0; k < v.size(); ++k) {
+      int32_t* r = out + off + static_cast<int64_t>(k) * kRec;
+      r[0] = v[k].seq;
+      r[1] = v[k].tok0;
+      r[2] = v[k].n_q;
+      r[3] = v[k].pb;
+      r[4] = v[k].pe;
+      r[5] = v[k].part_row;
+    }
+  };
+  put(off_decode, dec);
+  put(off_tile, til);
+  for (size_t k = 0; k < comb.size(); ++k) {
+    int32_t* r = out + off_combine + static_cast<int64_t>(k) * kRec;
+    r[0] = comb[k].seq;
+    r[1] = comb[k].tok0;
+    r[2] = comb[k].n_q;
+    r[3] = comb[k].pb;
+    r[4] = comb[k].pe;
+  }
+
+  info->num_seqs = num_seqs;
+  info->num_tokens = num_tokens;
+  info->n_decode_items = static_cast<int32_t>(dec.size());
+  info->n_tile_items = static_cast<int32_t>(til.size());
+  info->n_combine = static_cast<int32_t>(comb.size());
+  info->off_seqs = static_cast<int32_t>(off_seqs);
+  info->off_tables = static_cast<int32_t>(off_tables);
+  info->off_decode = static_cast<int32_t>(off_decode);
+  info->off_tile = static_cast<int32_t>(off_tile);
+  info->off_combine = static_cast<int32_t>(off_combine);
+  info->total_ints = static_cast<int32_t>(total);
+  info->pages_per_split = split;
+  info->part_rows = part_rows;
+  info->total_pages = total_pages;
+  // ws_o [part_rows][KVH][128] fp32 then ws_lse [part_rows][KVH]; KVH is not known here, so the
+  // size is reported per KV head and scaled by the attention call.
+  info->workspace_bytes_per_kv_head = part_rows * (128 + 1) * 4;
+  return MS_OK;
+}

@@ -1,0 +1,109 @@
+"""Host planner (ms_plan_build) properties: complete, disjoint page coverage; decode/tile split;
+longest-first order; consistent split-KV partial rows; clear errors on bad batches."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from miniserve_b200.attention import SeqChunk, plan_batch
+from miniserve_b200.workloads import config1, config2, config3, config4, custom
+
+REC = 8
+
+
+def decode_plan(packed: np.ndarray, info):
+    def recs(off: int, n: int) -> np.ndarray:
+        return packed[off : off + n * REC].reshape(n, REC)
+
+    return (recs(info.off_seqs, info.num_seqs), recs(info.off_decode, info.n_decode_items),
+            recs(info.off_tile, info.n_tile_items), recs(info.off_combine, info.n_combine))
+
+
+def check_plan(chunks: list[SeqChunk], num_tokens: int, split: int = 0) -> None:
+    packed, info = plan_batch(chunks, num_tokens, 16, 148, split)
+    seqs, dec, til, comb = decode_plan(packed, info)
+    assert info.num_seqs == len(chunks)
+    flat_tables = packed[info.off_tables :]
+    for i, c in enumerate(chunks):
+        r = seqs[i]
+        assert list(r[:4]) == [c.flat_start, c.num_new, c.num_cached, c.context_len]
+        assert list(flat_tables[r[4] : r[4] + r[5]]) == list(c.block_table)
+    # Every query tile's visible pages are covered exactly once by its items.
+    cover: dict[tuple[int, int], list[tuple[int, int, int]]] = {}
+    for kind, items in (("dec", dec), ("til", til)):
+        for it in items:
+            seq, tok0, nq, pb, pe, part = (int(x) for x in it[:6])
+            c = chunks[seq]
+            assert 0 < nq and tok0 + nq <= c.num_new
+            assert 0 <= pb < pe
+            if kind == "dec":
+                assert c.num_new <= 8 and tok0 == 0 and nq == c.num_new
+            else:
+                assert c.num_new > 8 and tok0 % 64 == 0 and nq == min(64, c.num_new - tok0)
+            cover.setdefault((seq, tok0), []).append((pb, pe, part))
+        lens = [int(it[4] - it[3]) for it in items]
+        assert lens == sorted(lens, reverse=True), "items must be longest first"
+    combos = {(int(r[0]), int(r[1])): r for r in comb}
+    for c_idx, c in enumerate(chunks):
+        step = 8 if c.num_new <= 8 else 64
+        for tok0 in range(0, c.num_new, step):
+            nq = min(step, c.num_new - tok0)
+            pages = -(-(c.num_cached + tok0 + nq) // 16)
+            spans = sorted(cover.pop((c_idx, tok0)))
+            assert spans[0][0] == 0 and spans[-1][1] == pages
+            for a, b in zip(spans, spans[1:]):
+                assert a[1] == b[0]
+            if len(spans) == 1:
+                assert spans[0][2] == -1 and (c_idx, tok0) not in combos
+            else:
+                r = combos[(c_idx, tok0)]
+                assert int(r[2]) == nq and int(r[4]) == len(spans)
+                parts = sorted(s[2] for s in spans)
+                assert parts == [int(r[3]) + k * 2 * nq for k in range(len(spans))]
+    assert not cover
+    assert info.workspace_bytes_per_kv_head == info.part_rows * 129 * 4
+
+
+@pytest.mark.parametrize("make", [config1, config2, config3, config4])
+@pytest.mark.parametrize("split", [0, 1, 7, 64])
+def test_plan_covers_benchmark_batches(make, split: int) -> None:
+    b = make(seed=3)
+    check_plan(b.chunks, b.num_tokens, split)
+
+
+@pytest.mark.parametrize("seed", range(5))
+def test_plan_random_ragged_batches(seed: int) -> None:
+    rng = np.random.default_rng(seed)
+    rows = []
+    for _ in range(int(rng.integers(1, 40))):
+        kind = rng.integers(0, 4)
+        n = 1 if kind == 0 else int(rng.integers(2, 9)) if kind == 1 else int(rng.integers(9, 300))
+        rows.append((n, int(rng.integers(0, 3000))))
+    b = custom(rows, seed=seed)
+    check_plan(b.chunks, b.num_tokens, int(rng.integers(0, 20)))
+
+
+def test_empty_batch() -> None:
+    packed, info = plan_batch([], 0)
+    assert info.n_decode_items == info.n_tile_items == info.n_combine == 0
+
+
+def test_plan_rejects_short_table() -> None:
+    with pytest.raises(ValueError, match="blocks but its table has"):
+        plan_batch([SeqChunk(0, 1, 40, [0, 1])], 1)
+
+
+def test_plan_rejects_zero_new_tokens() -> None:
+    with pytest.raises(ValueError, match="invalid"):
+        plan_batch([SeqChunk(0, 0, 4, [0])], 1)
+
+
+def test_plan_rejects_rows_outside_batch() -> None:
+    with pytest.raises(ValueError, match="invalid"):
+        plan_batch([SeqChunk(5, 4, 0, [0])], 6)
+
+
+def test_plan_rejects_other_block_sizes() -> None:
+    with pytest.raises(ValueError, match="block_size"):
+        plan_batch([SeqChunk(0, 1, 0, [0])], 1, block_size=32)
