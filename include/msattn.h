@@ -124,6 +124,32 @@ MS_API int ms_paged_attention(const void* q, int64_t q_row_stride, void* out, in
                        const MsPlanInfo* plan, void* workspace, int64_t workspace_bytes,
                        float scale, void* stream);
 
+/* ---- Attention for callers that cannot allocate device memory -------------------------------
+ * No counterpart in the reference (MiniServe allocates everything through PyTorch).
+ *
+ * Same work and arguments as ms_paged_attention, minus the workspace: the split-KV partials go
+ * to a fixed scratch array compiled into the library, MS_NOALLOC_SCRATCH_BYTES on every GPU that
+ * loads it, held until the process exits.  It is meant for hosts that never let a plugin call
+ * cudaMalloc (an engine that gives all GPU memory to its own arena, a custom-op interface with
+ * no allocator hook, a loop that cannot take cudaMalloc's implicit synchronisation).  The call
+ * itself allocates nothing.
+ *
+ *  - A plan needing more than MS_NOALLOC_SCRATCH_BYTES of partials
+ *    (plan->workspace_bytes_per_kv_head * num_kv_heads) is rejected with MS_ERR_CAPACITY; plan
+ *    with a larger pages_per_split or use ms_paged_attention.
+ *  - The first call on a device looks up that device's address of the array (with that device
+ *    current); make that first call before any stream capture.
+ *  - All calls share the array: calls that overlap on the GPU race on it; calls ordered on one
+ *    stream are safe.  No state carries over between calls. */
+#define MS_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)
+
+MS_API int ms_paged_attention_noalloc(const void* q, int64_t q_row_stride, void* out,
+                                      int64_t out_row_stride, int32_t num_heads,
+                                      int32_t num_kv_heads, const void* k_cache,
+                                      const void* v_cache, int32_t num_blocks,
+                                      const int32_t* plan_dev, const MsPlanInfo* plan,
+                                      float scale, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

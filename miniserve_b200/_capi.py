@@ -35,6 +35,7 @@ EXPORTED = (
     "ms_qk_norm_rope_scatter",
     "ms_kv_scatter",
     "ms_paged_attention",
+    "ms_paged_attention_noalloc",
 )
 
 
@@ -82,6 +83,10 @@ _SIGNATURES = {
         C.c_int,
         [_P, _I64, _P, _I64, _I32, _I32, _P, _P, _I32, _P, C.POINTER(MsPlanInfo), _P, _I64,
          C.c_float, _P],
+    ),
+    "ms_paged_attention_noalloc": (
+        C.c_int,
+        [_P, _I64, _P, _I64, _I32, _I32, _P, _P, _I32, _P, C.POINTER(MsPlanInfo), C.c_float, _P],
     ),
 }
 

@@ -18,7 +18,7 @@ CSRC = PKG / "csrc"
 LIB_DIR = PKG / "_lib"
 LIB = LIB_DIR / "libmsattn.so"
 
-SOURCES = [CSRC / "msattn.cu", CSRC / "plan.cpp"]
+SOURCES = [CSRC / "msattn.cu", CSRC / "plan.cpp", CSRC / "noalloc.cu"]
 DEPS = [*SOURCES, *CSRC.glob("*.cuh"), ROOT / "include" / "msattn.h"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
