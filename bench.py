@@ -50,6 +50,11 @@ def parse() -> argparse.Namespace:
     p.add_argument("--seqs", type=int, default=256)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--pages-per-split", type=int, default=0)
+    p.add_argument("--layers", type=int, default=LAYERS,
+                   help="layers per step (28 for the headline; fewer only for small profiles)")
+    p.add_argument("--workload", choices=["cfg2", "cfg3", "cfg4"], default="cfg2",
+                   help="cfg2 is the headline; cfg3 (mixed prefill) and cfg4 (prefix + verify) "
+                        "are reported alongside")
     return p.parse_args()
 
 
@@ -119,19 +124,22 @@ class ClockSampler:
 # ---------------------------------------------------------------------------------------------
 
 
-def attention_bytes(batch) -> tuple[int, int]:
-    """Algorithmic bytes of one attention launch (kernels B+C) and of one kernel-A launch.
+def attention_bytes(batch) -> tuple[int, int, int]:
+    """Algorithmic bytes of one attention launch (kernels B+C), of one kernel-A launch, and the
+    attention FLOPs (causal pairs only).
 
-    Attention: every context token's K and V of each KV head once (bf16), the queries in and the
-    outputs out, and the block-table entries.  Kernel A: the qkv row read, q written, K and V
-    written to the pool, cos/sin rows and the slot/position indices.
+    Attention bytes: every distinct physical KV block's K and V of each KV head once (bf16; a
+    shared prefix block counts once), the queries in and the outputs out, and the block-table
+    entries.  Kernel A: the qkv row read, q written, K and V written to the pool, cos/sin rows and
+    the slot/position indices.  FLOPs: 4 * 128 * 16 heads per (query token, visible key).
     """
-    ctx = sum(c.context_len for c in batch.chunks)
+    kv_tokens = batch.unique_kv_tokens()
     t = batch.num_tokens
     tables = sum(-(-c.context_len // 16) for c in batch.chunks)
-    attn = ctx * KVH * D * 2 * 2 + t * H * D * 2 * 2 + tables * 4
+    attn = kv_tokens * KVH * D * 2 * 2 + t * H * D * 2 * 2 + tables * 4
     kern_a = t * (H + 2 * KVH) * D * 2 + t * H * D * 2 + t * 2 * KVH * D * 2 + t * D * 4 * 2 + t * 8
-    return attn, kern_a
+    pairs = sum(c.num_new * c.num_cached + c.num_new * (c.num_new + 1) // 2 for c in batch.chunks)
+    return attn, kern_a, 4 * D * H * pairs
 
 
 def run_ours(args: argparse.Namespace, rank: int, world: int, device: torch.device) -> dict:
@@ -139,9 +147,15 @@ def run_ours(args: argparse.Namespace, rank: int, world: int, device: torch.devi
     from miniserve_b200.attention import attend, build_attention_metadata
     from miniserve_b200.kv_pool import allocate_kv_cache
     from miniserve_b200.qwen3_attention import qk_norm_rope_scatter
-    from miniserve_b200.workloads import config2, rope_tables
+    from miniserve_b200.workloads import config2, config3, config4, rope_tables
 
-    batch = config2(seed=1000 + rank, num_seqs=args.seqs)
+    if args.workload == "cfg2":
+        batch = config2(seed=1000 + rank, num_seqs=args.seqs)
+    elif args.workload == "cfg3":
+        batch = config3(seed=1000 + rank)
+    else:
+        batch = config4(seed=1000 + rank)
+    LAYERS = args.layers
     t = batch.num_tokens
     g = torch.Generator(device=device).manual_seed(1234 + rank)
     pool, views = allocate_kv_cache(LAYERS, batch.num_blocks, KVH, device, zero=False)
@@ -247,15 +261,17 @@ def run_ours(args: argparse.Namespace, rank: int, world: int, device: torch.devi
     h2d = qkv_host.numel() * 2 + pos_host.numel() * 8 + slot_host.numel() * 8 + int(info.total_ints) * 4
     d2h = out_host.numel() * 2
 
-    attn_bytes, a_bytes = attention_bytes(batch)
+    attn_bytes, a_bytes, attn_flops = attention_bytes(batch)
     return {
         "total_ms": total_ms,
         "e2e_ms": e2e_ms,
         "attn_ms": float(np.mean(attn_ms)),
         "attn_bytes": attn_bytes,
+        "attn_flops": attn_flops,
+        "logical_kv_tokens": batch.kv_tokens_read(),
         "kernel_a_bytes": a_bytes,
         "tokens": t,
-        "kv_tokens": batch.kv_tokens_read(),
+        "kv_tokens": batch.unique_kv_tokens(),
         "num_blocks": batch.num_blocks,
         "clocks": clocks,
         "launches_per_step": LAYERS * launches_per_layer,
@@ -388,7 +404,8 @@ def main() -> None:
     tokens_all = r["tokens"] * world
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if (rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload == "cfg2"
+            and args.layers == LAYERS):
         t_layer, t, threads, n = run_cpu_layers(args.seqs, 1, None, 12.0)
         cpu = {"value": t / (LAYERS * t_layer), "unit": "tok/s", "cores": threads, "kind": "port",
                "sample": f"1 of 28 layers of the full config-2 batch, {n} timed runs on the host "
@@ -402,8 +419,9 @@ def main() -> None:
         traffic = None
         if traffic_file.exists():
             traffic = json.loads(traffic_file.read_text()).get("paged_attn_decode_cfg2")
+        metric = METRIC if args.workload == "cfg2" else METRIC.replace("config 2", args.workload)
         line = {
-            "metric": METRIC,
+            "metric": metric,
             "value": tokens_all / (ms_per_step * 1e-3),
             "unit": "tok/s",
             "n_gpus": world,
@@ -416,14 +434,17 @@ def main() -> None:
             "dtype": "bf16",
             "data": "synthetic",
             "config": {
-                "workload": f"config2: {args.seqs} decode seqs/GPU, ctx U[256,4096], 16q/8kv "
-                            "heads, d128, block 16, 28 layers",
+                "workload": (f"config2: {args.seqs} decode seqs/GPU, ctx U[256,4096], 16q/8kv "
+                             f"heads, d128, block 16, {args.layers} layers"
+                             if args.workload == "cfg2" else args.workload),
+                "layers": args.layers,
                 "kv_tokens_per_layer": r["kv_tokens"],
+                "logical_kv_tokens_per_layer": r["logical_kv_tokens"],
                 "pool_blocks_per_layer": r["num_blocks"],
                 "l2": "inputs larger than L2 (KV read per layer-step >> 126 MB)",
                 "parallelism": f"sequence-sharded x{world}, no data-path collective",
             },
-            "us_per_layer_step": ms_per_step * 1e3 / LAYERS,
+            "us_per_layer_step": ms_per_step * 1e3 / args.layers,
             "attn_us_per_layer": attn_ms * 1e3,
             "roofline": {
                 "kernel": "paged attention decode (kernel B + combine C)",
@@ -435,6 +456,7 @@ def main() -> None:
                 "frac": achieved / hbm,
                 "traffic": traffic,
                 "algorithmic_bytes_per_launch": r["attn_bytes"],
+                "attn_tflops": r["attn_flops"] / (attn_ms * 1e-3) / 1e12,
             },
             "cpu_baseline": cpu,
             "e2e": {"value": tokens_all / (e2e_per_step * 1e-3), "unit": "tok/s",
