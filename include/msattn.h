@@ -66,7 +66,7 @@ typedef struct MsPlanInfo {
   int32_t num_seqs;
   int32_t num_tokens;
   int32_t n_decode_items;  /* work items of <= 8 query tokens (decode / speculative verify) */
-  int32_t n_tile_items;    /* work items of up to 64 query tokens of a longer chunk */
+  int32_t n_tile_items;    /* work items of 9..64-token chunks (mma.sync tile kernel) */
   int32_t n_combine;       /* split tiles whose partials must be merged */
   int32_t off_seqs;        /* int32 offsets of each section inside the packed buffer */
   int32_t off_tables;
@@ -80,7 +80,10 @@ typedef struct MsPlanInfo {
                                           ms_paged_attention wants this x num_kv_heads bytes
                                           (0 when no tile is split) */
   int64_t total_pages;     /* sum over work tiles of KV pages read (per KV head) */
-  int32_t reserved[8];
+  int32_t n_tc_items;      /* work items of 64 query tokens of chunks longer than 64 tokens,
+                              run on the tcgen05 tensor-core kernel */
+  int32_t off_tc;
+  int32_t reserved[6];
 } MsPlanInfo;
 
 /* Upper bound on the packed buffer length (int32 elements) for a batch of this size. */

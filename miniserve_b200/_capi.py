@@ -56,7 +56,9 @@ class MsPlanInfo(C.Structure):
         ("part_rows", C.c_int64),
         ("workspace_bytes_per_kv_head", C.c_int64),
         ("total_pages", C.c_int64),
-        ("reserved", C.c_int32 * 8),
+        ("n_tc_items", C.c_int32),
+        ("off_tc", C.c_int32),
+        ("reserved", C.c_int32 * 6),
     ]
 
 

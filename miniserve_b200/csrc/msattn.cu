@@ -15,6 +15,7 @@
 #include "ms_common.cuh"
 #include "norm_rope_scatter.cuh"
 #include "paged_attention.cuh"
+#include "prefill_tc.cuh"
 
 namespace ms_host {
 
@@ -48,14 +49,17 @@ struct MapKey {
   uintptr_t base;
   int num_blocks;
   int num_kv;
+  int box;  // 0: whole (block, head) page pair; 1: one 2 KiB quarter (K lo/hi, V lo/hi)
   bool operator==(const MapKey& o) const {
-    return device == o.device && base == o.base && num_blocks == o.num_blocks && num_kv == o.num_kv;
+    return device == o.device && base == o.base && num_blocks == o.num_blocks &&
+           num_kv == o.num_kv && box == o.box;
   }
 };
 struct MapKeyHash {
   size_t operator()(const MapKey& k) const {
     return std::hash<uintptr_t>()(k.base) ^ (static_cast<size_t>(k.num_blocks) << 20) ^
-           (static_cast<size_t>(k.device) << 56) ^ static_cast<size_t>(k.num_kv);
+           (static_cast<size_t>(k.device) << 56) ^ static_cast<size_t>(k.num_kv) ^
+           (static_cast<size_t>(k.box) << 40);
   }
 };
 
@@ -63,12 +67,15 @@ static std::mutex g_map_mutex;
 static std::unordered_map<MapKey, CUtensorMap, MapKeyHash> g_maps;
 
 // One layer's pool region viewed as a 5-D tensor {64 dims, 16 tokens, 4 quarters (K lo, K hi,
-// V lo, V hi), KV heads, blocks}; one box is a whole 8 KiB (block, head) page pair.
-static int kv_tensor_map(const void* k_cache, int num_blocks, int num_kv, CUtensorMap* out) {
+// V lo, V hi), KV heads, blocks}.  Box kind 0 is a whole 8 KiB (block, head) page pair (decode
+// kernel); box kind 1 is one 2 KiB quarter, so the tensor-core kernel can lay 8 pages' K and V
+// out as contiguous 128-key operand tiles.
+static int kv_tensor_map(const void* k_cache, int num_blocks, int num_kv, int box_kind,
+                         CUtensorMap* out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail("cudaGetDevice", e);
-  const MapKey key{dev, reinterpret_cast<uintptr_t>(k_cache), num_blocks, num_kv};
+  const MapKey key{dev, reinterpret_cast<uintptr_t>(k_cache), num_blocks, num_kv, box_kind};
   std::lock_guard<std::mutex> lock(g_map_mutex);
   auto it = g_maps.find(key);
   if (it != g_maps.end()) {
@@ -84,7 +91,7 @@ static int kv_tensor_map(const void* k_cache, int num_blocks, int num_kv, CUtens
                               static_cast<cuuint64_t>(num_blocks)};
   const cuuint64_t strides[4] = {128, 2048, ms::kPageKVBytes,
                                  static_cast<cuuint64_t>(num_kv) * ms::kPageKVBytes};
-  const cuuint32_t box[5] = {64, 16, 4, 1, 1};
+  const cuuint32_t box[5] = {64, 16, box_kind == 0 ? 4u : 1u, 1, 1};
   const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
   CUtensorMap map;
   const CUresult r = fn(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, const_cast<void*>(k_cache), dims,
@@ -107,6 +114,7 @@ constexpr int kDecodeWarps = 4, kDecodeStages = 8;
 constexpr int kTileWarps = 8, kTileStages = 8;
 using DecodeCfg = ms::AttnCfg<0, kDecodeWarps, kDecodeStages>;
 using TileCfg = ms::AttnCfg<1, kTileWarps, kTileStages>;
+static_assert(ms::TcCfg::kSmemBytes <= 232448, "tensor-core kernel exceeds 227 KiB of smem");
 
 static int ensure_smem_attrs() {
   // Per device: the attribute is a property of the function on the current device.
@@ -124,6 +132,9 @@ static int ensure_smem_attrs() {
   e = cudaFuncSetAttribute(ms::paged_attn_kernel<1, kTileWarps, kTileStages>,
                            cudaFuncAttributeMaxDynamicSharedMemorySize, TileCfg::kSmemBytes);
   if (e != cudaSuccess) return cuda_fail("cudaFuncSetAttribute(tile)", e);
+  e = cudaFuncSetAttribute(ms::prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           ms::TcCfg::kSmemBytes);
+  if (e != cudaSuccess) return cuda_fail("cudaFuncSetAttribute(tc)", e);
   done[dev] = true;
   return MS_OK;
 }
@@ -317,7 +328,8 @@ extern "C" int ms_paged_attention(const void* q, int64_t q_row_stride, void* out
     set_error("ms_paged_attention: need a plan and num_heads == 2 * num_kv_heads > 0");
     return MS_ERR_ARG;
   }
-  const int64_t n_items = static_cast<int64_t>(plan->n_decode_items) + plan->n_tile_items;
+  const int64_t n_items = static_cast<int64_t>(plan->n_decode_items) + plan->n_tile_items +
+                          plan->n_tc_items;
   if (n_items == 0) return MS_OK;
   int rc = check_pool(k_cache, v_cache, num_blocks, num_kv_heads);
   if (rc) return rc;
@@ -341,8 +353,13 @@ extern "C" int ms_paged_attention(const void* q, int64_t q_row_stride, void* out
   rc = ensure_smem_attrs();
   if (rc) return rc;
   CUtensorMap map;
-  rc = kv_tensor_map(k_cache, num_blocks, num_kv_heads, &map);
+  rc = kv_tensor_map(k_cache, num_blocks, num_kv_heads, 0, &map);
   if (rc) return rc;
+  CUtensorMap qmap;
+  if (plan->n_tc_items > 0) {
+    rc = kv_tensor_map(k_cache, num_blocks, num_kv_heads, 1, &qmap);
+    if (rc) return rc;
+  }
 
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
   ms::AttnArgs a;
@@ -366,6 +383,14 @@ extern "C" int ms_paged_attention(const void* q, int64_t q_row_stride, void* out
         <<<plan->n_decode_items * num_kv_heads, DecodeCfg::kThreads, DecodeCfg::kSmemBytes, s>>>(map, a);
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail("paged_attn decode launch", e);
+  }
+  if (plan->n_tc_items > 0) {
+    a.items = plan_dev + plan->off_tc;
+    a.n_items = plan->n_tc_items;
+    ms::prefill_tc_kernel<<<plan->n_tc_items * num_kv_heads, ms::TcCfg::kThreads,
+                            ms::TcCfg::kSmemBytes, s>>>(qmap, a);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail("prefill_tc launch", e);
   }
   if (plan->n_tile_items > 0) {
     a.items = plan_dev + plan->off_tile;

@@ -6,7 +6,9 @@
 // slot lists and shifted causal masks.  Here nothing is padded or gathered: each sequence keeps
 // its own block table (CSR), and the work is cut into (query tile, KV page range) items:
 //   * a sequence with <= 8 new tokens (decode, speculative verify) is one decode tile;
-//   * a longer chunk is cut into tiles of 64 query tokens;
+//   * a chunk of 9..64 tokens is one tile for the mma.sync tile kernel;
+//   * a chunk of more than 64 tokens is cut into tiles of 64 query tokens for the tcgen05
+//     tensor-core kernel, whose page ranges are split in whole 128-key blocks (8 pages);
 //   * a tile's visible pages, ceil((num_cached + tok0 + n_q) / 16), are split into near-equal
 //     ranges of at most `pages_per_split` pages; split tiles get partial rows in the workspace
 //     and a combine record.
@@ -29,6 +31,8 @@ constexpr int kRec = 8;
 constexpr int kDecodeMaxTokens = 8;  // backends.py:32 SHORT_QUERY: the batched (short) path
 constexpr int kTileTokens = 64;      // query tokens per tile-mode work item (128 rows)
 constexpr int kItemsPerSm = 4;       // automatic split size aims at this many items per SM
+constexpr int kTcBlockPages = 8;     // 128-key blocks of the tensor-core kernel
+constexpr int kTcMinSplitPages = 32; // tensor-core items cover at least 4 blocks
 
 struct Item {
   int seq, tok0, n_q, pb, pe, part_row;
@@ -46,7 +50,7 @@ extern "C" int64_t ms_plan_capacity(int32_t num_seqs, int32_t num_tokens,
   const int64_t tiles = static_cast<int64_t>(num_seqs) + num_tokens / kTileTokens + 1;
   const int64_t items = tiles + total_table_entries;
   return round4(static_cast<int64_t>(num_seqs) * kRec) + round4(total_table_entries) +
-         2 * round4(items * kRec) + round4(tiles * kRec) + 16;
+         3 * round4(items * kRec) + round4(tiles * kRec) + 16;
 }
 
 extern "C" int ms_plan_build(int32_t num_seqs, const int32_t* flat_start, const int32_t* num_new,
@@ -116,12 +120,16 @@ extern "C" int ms_plan_build(int32_t num_seqs, const int32_t* flat_start, const 
     split = static_cast<int>(std::clamp<int64_t>((total_pages + target - 1) / std::max<int64_t>(target, 1), 8, 512));
   }
 
-  std::vector<Item> dec, til, comb;
+  std::vector<Item> dec, til, tcv, comb;
   int64_t part_rows = 0;
+  const int tc_split = std::max(kTcMinSplitPages, (split + kTcBlockPages - 1) / kTcBlockPages * kTcBlockPages);
   for (const Item& t : tiles) {
     const int pages = t.pe;
-    const int ns = (pages + split - 1) / split;
-    std::vector<Item>& dst = t.n_q <= kDecodeMaxTokens && num_new[t.seq] <= kDecodeMaxTokens ? dec : til;
+    const int nn = num_new[t.seq];
+    const bool is_tc = nn > kTileTokens;
+    const int sp = is_tc ? tc_split : split;
+    const int ns = (pages + sp - 1) / sp;
+    std::vector<Item>& dst = nn <= kDecodeMaxTokens ? dec : (is_tc ? tcv : til);
     if (ns <= 1) {
       dst.push_back({t.seq, t.tok0, t.n_q, 0, pages, -1});
       continue;
@@ -131,10 +139,13 @@ extern "C" int ms_plan_build(int32_t num_seqs, const int32_t* flat_start, const 
       ms_host::set_error("ms_plan_build: too many partial rows");
       return MS_ERR_PLAN;
     }
-    const int base = pages / ns, rem = pages % ns;
+    // Near-equal ranges; tensor-core ranges stay whole 128-key blocks except the last.
+    const int unit = is_tc ? kTcBlockPages : 1;
+    const int units = (pages + unit - 1) / unit;
+    const int base = units / ns, rem = units % ns;
     int pb = 0;
     for (int s = 0; s < ns; ++s) {
-      const int len = base + (s < rem ? 1 : 0);
+      const int len = std::min(pages - pb, (base + (s < rem ? 1 : 0)) * unit);
       dst.push_back({t.seq, t.tok0, t.n_q, pb, pb + len,
                      static_cast<int>(part_rows + static_cast<int64_t>(s) * rows)});
       pb += len;
@@ -145,12 +156,14 @@ extern "C" int ms_plan_build(int32_t num_seqs, const int32_t* flat_start, const 
   auto longest_first = [](const Item& x, const Item& y) { return (x.pe - x.pb) > (y.pe - y.pb); };
   std::stable_sort(dec.begin(), dec.end(), longest_first);
   std::stable_sort(til.begin(), til.end(), longest_first);
+  std::stable_sort(tcv.begin(), tcv.end(), longest_first);
 
   const int64_t off_seqs = 0;
   const int64_t off_tables = round4(off_seqs + static_cast<int64_t>(num_seqs) * kRec);
   const int64_t off_decode = round4(off_tables + total_entries);
   const int64_t off_tile = round4(off_decode + static_cast<int64_t>(dec.size()) * kRec);
-  const int64_t off_combine = round4(off_tile + static_cast<int64_t>(til.size()) * kRec);
+  const int64_t off_tc = round4(off_tile + static_cast<int64_t>(til.size()) * kRec);
+  const int64_t off_combine = round4(off_tc + static_cast<int64_t>(tcv.size()) * kRec);
   const int64_t total = round4(off_combine + static_cast<int64_t>(comb.size()) * kRec);
   if (total > out_capacity) {
     ms_host::set_error("ms_plan_build: output buffer holds " + std::to_string(out_capacity) +
@@ -185,6 +198,7 @@ extern "C" int ms_plan_build(int32_t num_seqs, const int32_t* flat_start, const 
   };
   put(off_decode, dec);
   put(off_tile, til);
+  put(off_tc, tcv);
   for (size_t k = 0; k < comb.size(); ++k) {
     int32_t* r = out + off_combine + static_cast<int64_t>(k) * kRec;
     r[0] = comb[k].seq;
@@ -203,6 +217,8 @@ extern "C" int ms_plan_build(int32_t num_seqs, const int32_t* flat_start, const 
   info->off_tables = static_cast<int32_t>(off_tables);
   info->off_decode = static_cast<int32_t>(off_decode);
   info->off_tile = static_cast<int32_t>(off_tile);
+  info->n_tc_items = static_cast<int32_t>(tcv.size());
+  info->off_tc = static_cast<int32_t>(off_tc);
   info->off_combine = static_cast<int32_t>(off_combine);
   info->total_ints = static_cast<int32_t>(total);
   info->pages_per_split = split;

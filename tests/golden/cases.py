@@ -61,16 +61,28 @@ def _batch(name: str) -> Batch:
         g = np.random.default_rng(14)
         rows = [(1, int(c)) for c in g.integers(700, 1300, size=24)]
         return custom(rows, seed=14, name=name)
+    if name == "prefill_bf16":
+        # chunks longer than 64 tokens (the tensor-core prefill path): over a non-aligned cache,
+        # a fresh prompt just over one 64-token tile, a chunk over a long cache; plus a decode row.
+        rows = [(80, 37), (66, 0), (1, 20), (70, 130)]
+        return custom(rows, seed=15, name=name)
     raise KeyError(name)
 
 
-CASES = ("cfg1_fp32", "mixed_bf16", "prefix_verify_bf16", "groups_bf16")
+CASES = ("cfg1_fp32", "mixed_bf16", "prefix_verify_bf16", "groups_bf16", "prefill_bf16")
+# Cases whose q/k/v arrays are stored as SHA-256 digests (only the attention output in full).
+COMPACT = ("prefill_bf16",)
 
 
 def make_inputs(name: str) -> CaseInputs:
     batch = _batch(name)
     dtype = torch.float32 if name.endswith("fp32") else torch.bfloat16
-    g = torch.Generator().manual_seed(sum(map(ord, name)))
+    return random_inputs(batch, sum(map(ord, name)), dtype)
+
+
+def random_inputs(batch: Batch, seed: int, dtype: torch.dtype = torch.bfloat16) -> CaseInputs:
+    """Seeded activations and pool contents for any batch geometry."""
+    g = torch.Generator().manual_seed(seed)
     t = batch.num_tokens
     slots = batch.num_blocks * 16
     qkv = torch.randn(t, (H + 2 * KVH) * D, generator=g).to(dtype)

@@ -26,7 +26,8 @@ HERE = Path(__file__).resolve().parent
 sys.path.insert(0, str(HERE.parents[1]))
 sys.path.insert(0, str(HERE))
 
-from cases import CASES, D, EPS, H, KVH, THETA, make_inputs  # noqa: E402
+from cases import CASES, COMPACT, D, EPS, H, KVH, THETA, make_inputs  # noqa: E402
+import hashlib  # noqa: E402
 
 
 def _as_np(t: torch.Tensor) -> np.ndarray:
@@ -63,7 +64,7 @@ def run_reference(name: str) -> dict[str, np.ndarray]:
         q, k = apply_rope(q, k, cos, sin)
         meta = build_attention_metadata(chunks, slot_mapping, 16)
         out = paged_attention(q, k, v, k_cache, v_cache, meta, D**-0.5)
-    return {
+    arrays = {
         "digest": np.frombuffer(inp.digest().encode(), dtype=np.uint8),
         "q_rot": _as_np(q),
         "k_rot": _as_np(k),
@@ -73,6 +74,12 @@ def run_reference(name: str) -> dict[str, np.ndarray]:
         "n_groups": np.asarray([len(meta.groups)]),
         "n_prefills": np.asarray([len(meta.prefills)]),
     }
+    if name in COMPACT:
+        for key in ("q_rot", "k_rot", "k_at_slots", "v_at_slots"):
+            digest = hashlib.sha256(np.ascontiguousarray(arrays[key]).tobytes()).hexdigest()
+            arrays[key + "_sha256"] = np.frombuffer(digest.encode(), dtype=np.uint8)
+            del arrays[key]
+    return arrays
 
 
 def main() -> None:
@@ -81,7 +88,10 @@ def main() -> None:
         raise SystemExit("set MINISERVE_SRC to the reference's src/ directory")
     sys.path.insert(0, src)
     torch.set_num_threads(os.cpu_count() or 1)
+    only = sys.argv[1:]
     for name in CASES:
+        if only and name not in only:
+            continue
         arrays = run_reference(name)
         np.savez_compressed(HERE / f"{name}.npz", **arrays)
         print(name, {k: v.shape for k, v in arrays.items()})

@@ -17,6 +17,9 @@ def load_golden(name: str, dtype: torch.dtype) -> dict[str, torch.Tensor | str]:
     z = np.load(GOLDEN / f"{name}.npz")
     out: dict[str, torch.Tensor | str] = {"digest": bytes(z["digest"]).decode()}
     for key in ("q_rot", "k_rot", "k_at_slots", "v_at_slots", "out"):
+        if key not in z.files:
+            out[key + "_sha256"] = bytes(z[key + "_sha256"]).decode()
+            continue
         a = z[key]
         if a.dtype == np.uint16:
             out[key] = torch.from_numpy(a.view(np.int16).copy()).view(torch.bfloat16)
@@ -45,4 +48,21 @@ def run_oracle(inp: CaseInputs) -> dict[str, torch.Tensor]:
             "out": out, "k_cache": k_cache, "v_cache": v_cache}
 
 
-__all__ = ["load_golden", "make_inputs", "oracle_meta", "run_oracle"]
+def tensor_sha256(t: torch.Tensor) -> str:
+    """SHA-256 of a tensor's bytes in the layout make_golden.py hashes (bf16 as uint16)."""
+    import hashlib
+
+    c = t.contiguous()
+    if c.dtype == torch.bfloat16:
+        c = c.view(torch.int16)
+    return hashlib.sha256(c.numpy().tobytes()).hexdigest()
+
+
+def matches(got: torch.Tensor, gold: dict, key: str) -> bool:
+    """Bit equality with a stored array, or with its stored digest for compact cases."""
+    if key in gold:
+        return torch.equal(got, gold[key])
+    return tensor_sha256(got) == gold[key + "_sha256"]
+
+
+__all__ = ["load_golden", "make_inputs", "matches", "oracle_meta", "run_oracle", "tensor_sha256"]

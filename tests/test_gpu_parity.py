@@ -15,8 +15,9 @@ from __future__ import annotations
 import pytest
 import torch
 
-from golden.cases import CASES, D, EPS, H, KVH, THETA
+from golden.cases import CASES, D, EPS, H, KVH, THETA, random_inputs
 from golden_io import load_golden, make_inputs, run_oracle
+from miniserve_b200.workloads import config3, custom
 from gpu_harness import bf16_ulp_diff, covered_rows, run_layer
 from oracle import attention_oracle as orc
 
@@ -40,14 +41,16 @@ def _fp32_reference_out(inp, q_rot_gpu: torch.Tensor, k_slots: torch.Tensor,
 
 @pytest.mark.parametrize("name", [c for c in CASES if c.endswith("bf16")])
 def test_kernel_a_matches_reference_bits(name: str, cuda_device: torch.device) -> None:
+    """Against the reference's CPU results (the oracle reproduces them bit for bit, see
+    test_oracle_golden.py, so its arrays stand in for cases stored as digests)."""
     inp = make_inputs(name)
-    gold = load_golden(name, inp.dtype)
+    ref = run_oracle(inp)
     got = run_layer(inp, cuda_device)
     assert int(got["status"]) == 0
     # V rows are copied: bit-exact.  K rows in the pool are exactly what kernel A computed.
-    assert torch.equal(got["v_at_slots"].cpu(), gold["v_at_slots"])
+    assert torch.equal(got["v_at_slots"].cpu(), ref["v_at_slots"])
     for key in ("q_rot", "k_at_slots"):
-        ulps = bf16_ulp_diff(got[key].cpu(), gold[key])
+        ulps = bf16_ulp_diff(got[key].cpu(), ref[key])
         assert int(ulps.max()) <= 1, key
         assert float((ulps > 0).float().mean()) <= 1e-3, key
 
@@ -88,7 +91,35 @@ def test_attention_matches_reference(name: str, pages_per_split: int,
     assert err32 <= ATOL, err32
 
 
-@pytest.mark.parametrize("name", ["mixed_bf16", "prefix_verify_bf16"])
+def _random_case_vs_fp32(batch, seed: int, pages_per_split: int, device: torch.device) -> float:
+    inp = random_inputs(batch, seed)
+    got = run_layer(inp, device, pages_per_split=pages_per_split)
+    assert int(got["status"]) == 0
+    rows = covered_rows(inp)
+    ref32 = _fp32_reference_out(inp, got["q_rot"], got["k_slots"], got["v_slots"])[rows]
+    return (got["out"].cpu()[rows].float() - ref32).abs().max().item()
+
+
+@pytest.mark.parametrize("pages_per_split", [0, 8, 64])
+def test_tensor_core_prefill_config3(pages_per_split: int, cuda_device: torch.device) -> None:
+    """Config 3's geometry: 48 decode rows + two 1000-token chunks over 512 cached tokens
+    (tcgen05 kernel for the chunks, decode kernel for the rest), against the fp32 oracle."""
+    err = _random_case_vs_fp32(config3(seed=7), 7, pages_per_split, cuda_device)
+    assert err <= ATOL, err
+
+
+@pytest.mark.parametrize("rows", [
+    [(65, 0)], [(128, 0)], [(129, 0)], [(200, 1)], [(64, 0), (65, 63)], [(300, 700), (1, 5)],
+    [(1000, 0)],
+], ids=["65", "128", "129", "200_over_1", "64_and_65", "300_over_700", "1000_fresh"])
+def test_tensor_core_prefill_edges(rows, cuda_device: torch.device) -> None:
+    """Tile and 128-key block boundaries of the tensor-core path (with forced splits too)."""
+    for split in (0, 8):
+        err = _random_case_vs_fp32(custom(rows, seed=len(rows)), 3, split, cuda_device)
+        assert err <= ATOL, (split, err)
+
+
+@pytest.mark.parametrize("name", ["mixed_bf16", "prefix_verify_bf16", "prefill_bf16"])
 def test_scatter_only_path_equals_fused(name: str, cuda_device: torch.device) -> None:
     """paged_attention(q, k, v, ...) (reference call shape) == the fused layer path."""
     inp = make_inputs(name)

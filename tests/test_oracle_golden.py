@@ -12,7 +12,7 @@ import pytest
 import torch
 
 from golden.cases import CASES, D
-from golden_io import load_golden, make_inputs, run_oracle
+from golden_io import load_golden, make_inputs, matches, run_oracle
 from oracle import attention_oracle as orc
 
 
@@ -23,7 +23,7 @@ def test_oracle_reproduces_reference_golden(name: str) -> None:
     assert inp.digest() == gold["digest"], "seeded input generation drifted"
     got = run_oracle(inp)
     for key in ("q_rot", "k_rot", "k_at_slots", "v_at_slots"):
-        assert torch.equal(got[key], gold[key]), key
+        assert matches(got[key], gold, key), key
     tol = 1e-6 if inp.dtype == torch.float32 else 1e-2
     torch.testing.assert_close(got["out"].float(), gold["out"].float(), atol=tol, rtol=0)
 

@@ -17,12 +17,13 @@ def decode_plan(packed: np.ndarray, info):
         return packed[off : off + n * REC].reshape(n, REC)
 
     return (recs(info.off_seqs, info.num_seqs), recs(info.off_decode, info.n_decode_items),
-            recs(info.off_tile, info.n_tile_items), recs(info.off_combine, info.n_combine))
+            recs(info.off_tile, info.n_tile_items), recs(info.off_tc, info.n_tc_items),
+            recs(info.off_combine, info.n_combine))
 
 
 def check_plan(chunks: list[SeqChunk], num_tokens: int, split: int = 0) -> None:
     packed, info = plan_batch(chunks, num_tokens, 16, 148, split)
-    seqs, dec, til, comb = decode_plan(packed, info)
+    seqs, dec, til, tcv, comb = decode_plan(packed, info)
     assert info.num_seqs == len(chunks)
     flat_tables = packed[info.off_tables :]
     for i, c in enumerate(chunks):
@@ -31,7 +32,7 @@ def check_plan(chunks: list[SeqChunk], num_tokens: int, split: int = 0) -> None:
         assert list(flat_tables[r[4] : r[4] + r[5]]) == list(c.block_table)
     # Every query tile's visible pages are covered exactly once by its items.
     cover: dict[tuple[int, int], list[tuple[int, int, int]]] = {}
-    for kind, items in (("dec", dec), ("til", til)):
+    for kind, items in (("dec", dec), ("til", til), ("tc", tcv)):
         for it in items:
             seq, tok0, nq, pb, pe, part = (int(x) for x in it[:6])
             c = chunks[seq]
@@ -39,8 +40,11 @@ def check_plan(chunks: list[SeqChunk], num_tokens: int, split: int = 0) -> None:
             assert 0 <= pb < pe
             if kind == "dec":
                 assert c.num_new <= 8 and tok0 == 0 and nq == c.num_new
+            elif kind == "til":
+                assert 8 < c.num_new <= 64 and tok0 == 0 and nq == c.num_new
             else:
-                assert c.num_new > 8 and tok0 % 64 == 0 and nq == min(64, c.num_new - tok0)
+                assert c.num_new > 64 and tok0 % 64 == 0 and nq == min(64, c.num_new - tok0)
+                assert pb % 8 == 0, "tensor-core ranges start on 128-key blocks"
             cover.setdefault((seq, tok0), []).append((pb, pe, part))
         lens = [int(it[4] - it[3]) for it in items]
         assert lens == sorted(lens, reverse=True), "items must be longest first"
