@@ -176,7 +176,8 @@ def run_ours(args: argparse.Namespace, rank: int, world: int, device: torch.devi
     stream = torch.cuda.current_stream(device)
     scale = D**-0.5
     info = meta.info
-    launches_per_layer = 1 + (info.n_decode_items > 0) + (info.n_tile_items > 0) + (info.n_combine > 0)
+    launches_per_layer = (1 + (info.n_decode_items > 0) + (info.n_tile_items > 0)
+                          + (info.n_tc_items > 0) + (info.n_combine > 0))
 
     ev_attn = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(LAYERS)]
 
@@ -278,7 +279,8 @@ def run_ours(args: argparse.Namespace, rank: int, world: int, device: torch.devi
         "h2d": h2d,
         "d2h": d2h,
         "plan": {"decode_items": info.n_decode_items, "tile_items": info.n_tile_items,
-                 "combine": info.n_combine, "pages_per_split": info.pages_per_split},
+                 "tc_items": info.n_tc_items, "combine": info.n_combine,
+                 "pages_per_split": info.pages_per_split},
     }
 
 

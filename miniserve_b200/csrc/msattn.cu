@@ -410,7 +410,7 @@ extern "C" int ms_paged_attention(const void* q, int64_t q_row_stride, void* out
     c.num_kv = num_kv_heads;
     c.ws_o = a.ws_o;
     c.ws_lse = a.ws_lse;
-    ms::combine_kernel<<<plan->n_combine * num_kv_heads, 128, 0, s>>>(c);
+    ms::combine_kernel<<<plan->n_combine * num_kv_heads, ms::kCombineThreads, 0, s>>>(c);
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail("combine launch", e);
   }

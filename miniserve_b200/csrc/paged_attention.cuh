@@ -416,7 +416,9 @@ struct CombineArgs {
 };
 
 // Kernel C: out = sum_s 2^(lse_s - M) * O_s / sum_s 2^(lse_s - M) for every split tile.
-__global__ void __launch_bounds__(128) combine_kernel(const CombineArgs a) {
+// One CTA per (split tile, KV head); thread = (row, 16-dim slice), 32 rows per pass.
+constexpr int kCombineThreads = 256;
+__global__ void __launch_bounds__(kCombineThreads) combine_kernel(const CombineArgs a) {
   const int ci = blockIdx.x / a.num_kv;
   const int kvh = blockIdx.x - ci * a.num_kv;
   const int* cr = a.combines + static_cast<long long>(ci) * kRec;
@@ -424,7 +426,7 @@ __global__ void __launch_bounds__(128) combine_kernel(const CombineArgs a) {
   const int flat_start = a.seqs[static_cast<long long>(seq) * kRec];
   const int rows = n_q * kGroup;
   const int dc = (threadIdx.x & 7) * 16;
-  for (int r = threadIdx.x >> 3; r < rows; r += 16) {
+  for (int r = threadIdx.x >> 3; r < rows; r += kCombineThreads / 8) {
     float mx = -INFINITY;
     for (int s = 0; s < n_splits; ++s)
       mx = fmaxf(mx, a.ws_lse[static_cast<long long>(part_row0 + s * rows + r) * a.num_kv + kvh]);

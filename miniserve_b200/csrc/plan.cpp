@@ -31,6 +31,7 @@ constexpr int kRec = 8;
 constexpr int kDecodeMaxTokens = 8;  // backends.py:32 SHORT_QUERY: the batched (short) path
 constexpr int kTileTokens = 64;      // query tokens per tile-mode work item (128 rows)
 constexpr int kItemsPerSm = 4;       // automatic split size aims at this many items per SM
+constexpr int kMinSplitPages = 32;   // a split streams at least 256 KiB per KV head
 constexpr int kTcBlockPages = 8;     // 128-key blocks of the tensor-core kernel
 constexpr int kTcMinSplitPages = 32; // tensor-core items cover at least 4 blocks
 
@@ -86,6 +87,7 @@ extern "C" int ms_plan_build(int32_t num_seqs, const int32_t* flat_start, const 
   std::vector<Item> tiles;
   tiles.reserve(num_seqs);
   int64_t total_pages = 0;
+  int64_t short_pages = 0;  // pages of tiles that run on the decode / small-tile kernels
   for (int i = 0; i < num_seqs; ++i) {
     const int64_t n = num_new[i], c = num_cached[i], f = flat_start[i];
     const int64_t tlen = table_offsets[i + 1] - table_offsets[i];
@@ -111,13 +113,17 @@ extern "C" int ms_plan_build(int32_t num_seqs, const int32_t* flat_start, const 
       const int pages = static_cast<int>((c + t0 + nq + block_size - 1) / block_size);
       tiles.push_back({i, static_cast<int>(t0), nq, 0, pages, -1});
       total_pages += pages;
+      if (n <= kTileTokens) short_pages += pages;
     }
   }
 
+  // Split size for the bandwidth-bound kernels: enough items to fill the GPU several times
+  // over, but never so short that a CTA's start-up latency dominates its streaming.
   int split = pages_per_split;
   if (split == 0) {
     const int64_t target = static_cast<int64_t>(num_sms) * kItemsPerSm;
-    split = static_cast<int>(std::clamp<int64_t>((total_pages + target - 1) / std::max<int64_t>(target, 1), 8, 512));
+    split = static_cast<int>(std::clamp<int64_t>((short_pages + target - 1) / std::max<int64_t>(target, 1),
+                                                 kMinSplitPages, 512));
   }
 
   std::vector<Item> dec, til, tcv, comb;
