@@ -131,11 +131,11 @@ def slots_for(chunk: SeqChunk, block_size: int) -> list[int]:
 
 def _page_lookup(tables: Tensor, length: int, block_size: int) -> Tensor:
     """Slot of every context position 0..length-1 through a table (backends.py:74-77)."""
-    pos = torch.arange(length)
+    pos = torch.arange(length, device=tables.device)
     return tables[..., pos // block_size] * block_size + pos % block_size
 
 
-def _short_group(chunks: list[SeqChunk], block_size: int) -> OracleGroup:
+def _short_group(chunks: list[SeqChunk], block_size: int, device: torch.device) -> OracleGroup:
     """Pad a set of short-query sequences into one batch (backends.py:101-132)."""
     q_len = max(c.num_new for c in chunks)
     n_blocks = -(-max(c.context_len for c in chunks) // block_size)
@@ -151,31 +151,35 @@ def _short_group(chunks: list[SeqChunk], block_size: int) -> OracleGroup:
         out_index.extend(c.flat_start + i for i in range(c.num_new))
         valid.extend(b * q_len + i for i in range(c.num_new))
     everyone_full = all(c.num_new == q_len for c in chunks)
-    key_pos = torch.arange(padded_len)
-    qp = torch.tensor(q_pos, dtype=torch.long)
+    idx = dict(dtype=torch.long, device=device)
+    key_pos = torch.arange(padded_len, device=device)
+    qp = torch.tensor(q_pos, **idx)
     return OracleGroup(
-        q_index=torch.tensor(q_index, dtype=torch.long),
-        valid_rows=None if everyone_full else torch.tensor(valid, dtype=torch.long),
-        out_index=torch.tensor(out_index, dtype=torch.long),
-        ctx_slots=_page_lookup(torch.tensor(tables, dtype=torch.long), padded_len, block_size),
+        q_index=torch.tensor(q_index, **idx),
+        valid_rows=None if everyone_full else torch.tensor(valid, **idx),
+        out_index=torch.tensor(out_index, **idx),
+        ctx_slots=_page_lookup(torch.tensor(tables, **idx), padded_len, block_size),
         mask=key_pos[None, None, :] <= qp[:, :, None],
     )
 
 
-def _long_chunk(c: SeqChunk, block_size: int) -> OraclePrefill:
+def _long_chunk(c: SeqChunk, block_size: int, device: torch.device) -> OraclePrefill:
     """A chunk with more than SHORT_QUERY queries (backends.py:135-142)."""
     end = c.flat_start + c.num_new
     if c.num_cached == 0:
         return OraclePrefill(c.flat_start, end, None, None)
     n_blocks = -(-c.context_len // block_size)
-    table = torch.tensor(c.block_table[:n_blocks], dtype=torch.long)
+    table = torch.tensor(c.block_table[:n_blocks], dtype=torch.long, device=device)
     ctx = _page_lookup(table, c.context_len, block_size)
-    mask = torch.ones(c.num_new, c.context_len, dtype=torch.bool).tril(c.num_cached)
+    mask = torch.ones(c.num_new, c.context_len, dtype=torch.bool, device=device).tril(c.num_cached)
     return OraclePrefill(c.flat_start, end, ctx, mask)
 
 
 def build_metadata(chunks: list[SeqChunk], slot_mapping: Tensor, block_size: int) -> OracleMeta:
-    """Group short rows longest-context-first under the gather cap (backends.py:80-98)."""
+    """Group short rows longest-context-first under the gather cap (backends.py:80-98).
+
+    Index tensors and masks live on the slot mapping's device, as in the reference."""
+    device = slot_mapping.device
     short = sorted(
         (c for c in chunks if c.num_new <= SHORT_QUERY), key=lambda c: c.context_len, reverse=True
     )
@@ -183,12 +187,12 @@ def build_metadata(chunks: list[SeqChunk], slot_mapping: Tensor, block_size: int
     pending: list[SeqChunk] = []
     for c in short:
         if pending and (len(pending) + 1) * pending[0].context_len > MAX_GATHER_TOKENS:
-            groups.append(_short_group(pending, block_size))
+            groups.append(_short_group(pending, block_size, device))
             pending = []
         pending.append(c)
     if pending:
-        groups.append(_short_group(pending, block_size))
-    longs = [_long_chunk(c, block_size) for c in chunks if c.num_new > SHORT_QUERY]
+        groups.append(_short_group(pending, block_size, device))
+    longs = [_long_chunk(c, block_size, device) for c in chunks if c.num_new > SHORT_QUERY]
     return OracleMeta(slot_mapping, groups, longs)
 
 
