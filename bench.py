@@ -50,6 +50,8 @@ def parse() -> argparse.Namespace:
     p.add_argument("--seqs", type=int, default=256)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--pages-per-split", type=int, default=0)
+    p.add_argument("--no-graph", action="store_true",
+                   help="time eager launches instead of replaying the captured step")
     p.add_argument("--layers", type=int, default=LAYERS,
                    help="layers per step (28 for the headline; fewer only for small profiles)")
     p.add_argument("--workload", choices=["cfg2", "cfg3", "cfg4"], default="cfg2",
@@ -199,22 +201,37 @@ def run_ours(args: argparse.Namespace, rank: int, world: int, device: torch.devi
     if status:
         raise RuntimeError(f"device status {status:#x} after warm-up")
 
+    # The whole 28-layer step is captured once as a CUDA graph (the C-ABI calls neither allocate
+    # nor synchronise) and replayed; the eager time is reported beside it.
+    graph = None
+    if not args.no_graph:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step()
+        for _ in range(2):
+            graph.replay()
+        torch.cuda.synchronize(device)
+
+    def timed(fn) -> float:
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize(device)
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(args.steps):
+            fn()
+        stop.record(stream)
+        torch.cuda.synchronize(device)
+        return start.elapsed_time(stop)
+
     # ---- timed region: device-resident inputs ----
     sampler = ClockSampler(device.index if device.index is not None else 0) if rank == 0 else None
-    if world > 1:
-        torch.distributed.barrier()
-    torch.cuda.synchronize(device)
     if sampler:
         sampler.start()
         time.sleep(0.3)
-    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     attn_ms: list[float] = []
-    start.record(stream)
-    for _ in range(args.steps):
-        step(timed_kernels=False)
-    stop.record(stream)
-    torch.cuda.synchronize(device)
-    total_ms = start.elapsed_time(stop)
+    eager_ms = timed(step)
+    total_ms = timed(graph.replay) if graph is not None else eager_ms
     # per-kernel durations (same work, events around each attention launch)
     for _ in range(max(1, min(args.steps, 5))):
         step(timed_kernels=True)
@@ -265,6 +282,8 @@ def run_ours(args: argparse.Namespace, rank: int, world: int, device: torch.devi
     attn_bytes, a_bytes, attn_flops = attention_bytes(batch)
     return {
         "total_ms": total_ms,
+        "eager_ms": eager_ms,
+        "graph": graph is not None,
         "e2e_ms": e2e_ms,
         "attn_ms": float(np.mean(attn_ms)),
         "attn_bytes": attn_bytes,
@@ -396,11 +415,11 @@ def main() -> None:
         torch.distributed.barrier()
 
     r = run_ours(args, rank, world, device)
-    ms = torch.tensor([r["total_ms"], r["e2e_ms"], r["attn_ms"]], dtype=torch.float64,
-                      device=device)
+    ms = torch.tensor([r["total_ms"], r["e2e_ms"], r["attn_ms"], r["eager_ms"]],
+                      dtype=torch.float64, device=device)
     if world > 1:
         torch.distributed.all_reduce(ms, op=torch.distributed.ReduceOp.MAX)
-    total_ms, e2e_ms, attn_ms = (float(x) for x in ms.cpu())
+    total_ms, e2e_ms, attn_ms, eager_ms = (float(x) for x in ms.cpu())
     ms_per_step = total_ms / args.steps
     e2e_per_step = e2e_ms / args.steps
     tokens_all = r["tokens"] * world
@@ -447,6 +466,8 @@ def main() -> None:
                 "parallelism": f"sequence-sharded x{world}, no data-path collective",
             },
             "us_per_layer_step": ms_per_step * 1e3 / args.layers,
+            "step_timing": "CUDA-graph replay of the captured step" if r["graph"] else "eager",
+            "eager_ms_per_step": eager_ms / args.steps,
             "attn_us_per_layer": attn_ms * 1e3,
             "roofline": {
                 "kernel": "paged attention decode (kernel B + combine C)",

@@ -264,8 +264,13 @@ extern "C" int ms_qk_norm_rope_scatter(const void* qkv, int64_t qkv_row_stride, 
   a.num_tokens = num_tokens;
   a.num_heads = num_heads;
   a.num_kv = num_kv_heads;
+  if (num_kv_heads % ms::kRowsPerWarp != 0) {
+    set_error("ms_qk_norm_rope_scatter: num_kv_heads must be a multiple of 8");
+    return MS_ERR_ARG;
+  }
   constexpr int kWarps = 8;
-  const long long warps = static_cast<long long>(num_tokens) * (num_heads + 2 * num_kv_heads);
+  const long long warps =
+      static_cast<long long>(num_tokens) * (num_heads + 2 * num_kv_heads) / ms::kRowsPerWarp;
   const long long blocks = (warps + kWarps - 1) / kWarps;
   if (blocks > 0x7fffffffLL) {
     set_error("ms_qk_norm_rope_scatter: batch too large");

@@ -3,9 +3,9 @@
 // (src/miniserve/model/qwen3.py:94-98 -> layers.py:18-22 and :56-65) and the scatter at the top of
 // paged_attention (src/miniserve/attention/backends.py:159-160).
 //
-// One warp handles one (token, head row) pair: rows 0..H-1 are query heads, H..H+KVH-1 key heads,
-// H+KVH..H+2*KVH-1 value heads, i.e. the 128-column blocks of the fused qkv projection in order.
-// Each lane owns 4 consecutive dims (one 8-byte load, one 8-byte store).
+// Rows 0..H-1 of a token are query heads, H..H+KVH-1 key heads, H+KVH..H+2*KVH-1 value heads,
+// i.e. the 128-column blocks of the fused qkv projection in order.  Each lane owns 4 consecutive
+// dims of a row (one 8-byte load, one 8-byte store).
 //
 // Rounding follows the reference exactly where the order is fixed by it: fp32 squares, fp32 mean,
 // rsqrt, fp32 multiply, round to bf16, bf16 weight multiply (rounded), bf16 cos/sin, bf16 products
@@ -55,55 +55,50 @@ __device__ __forceinline__ float bf16_round(float x) {
   return __bfloat162float(__float2bfloat16_rn(x));
 }
 
+// One warp handles 8 head rows of one token: warps 0-1 of a token take the 16 query heads, warp 2
+// the 8 key heads, warp 3 the 8 value heads (rows are the 128-column blocks of the fused
+// projection, in order), so every warp does one kind of work.  All 8 row loads are issued before
+// any arithmetic, and the token's cos/sin values are read once per warp.
+constexpr int kRowsPerWarp = 8;
+
 template <int kWarps>
 __global__ void __launch_bounds__(kWarps * 32)
     qk_norm_rope_scatter_kernel(const NormRopeArgs a, unsigned* status) {
   const int lane = threadIdx.x & 31;
+  const int warps_per_tok = (a.num_heads + 2 * a.num_kv) / kRowsPerWarp;
   const long long gw = static_cast<long long>(blockIdx.x) * kWarps + (threadIdx.x >> 5);
-  const int rows_per_tok = a.num_heads + 2 * a.num_kv;
-  const long long t = gw / rows_per_tok;
+  const long long t = gw / warps_per_tok;
   if (t >= a.num_tokens) return;
-  const int hr = static_cast<int>(gw - t * rows_per_tok);
+  const int row0 = static_cast<int>(gw - t * warps_per_tok) * kRowsPerWarp;
   const int d0 = lane * 4;
 
-  const uint2 raw =
-      *reinterpret_cast<const uint2*>(a.qkv + t * a.qkv_row_stride + hr * kHeadDim + d0);
+  uint2 raw[kRowsPerWarp];
+  const __nv_bfloat16* src = a.qkv + t * a.qkv_row_stride + row0 * kHeadDim + d0;
+#pragma unroll
+  for (int r = 0; r < kRowsPerWarp; ++r)
+    raw[r] = *reinterpret_cast<const uint2*>(src + r * kHeadDim);
 
-  if (hr >= a.num_heads + a.num_kv) {  // value head: a pure copy into the pool
-    const long long slot = a.slots[t];
-    if (slot < 0 || slot >= a.num_slots) {
+  const bool is_v = row0 >= a.num_heads + a.num_kv;
+  const bool is_q = row0 < a.num_heads;
+  long long slot = 0;
+  bool slot_ok = true;
+  if (!is_q) {
+    slot = a.slots[t];
+    slot_ok = slot >= 0 && slot < a.num_slots;
+    if (!slot_ok) {
       if (lane == 0) atomicOr(status, kErrSlot);
       return;
     }
-    const int h = hr - a.num_heads - a.num_kv;
-    __nv_bfloat16* dst =
-        a.k_pool + 2 * kBlockTokens * 64 + pool_offset(slot, h, d0, a.block_stride, a.head_stride);
-    *reinterpret_cast<uint2*>(dst) = raw;
+  }
+  if (is_v) {  // value heads: a pure copy into the pool
+    const int h0 = row0 - a.num_heads - a.num_kv;
+    __nv_bfloat16* vbase = a.k_pool + 2 * kBlockTokens * 64;
+#pragma unroll
+    for (int r = 0; r < kRowsPerWarp; ++r)
+      *reinterpret_cast<uint2*>(vbase + pool_offset(slot, h0 + r, d0, a.block_stride, a.head_stride)) = raw[r];
     return;
   }
 
-  const bool is_q = hr < a.num_heads;
-  const __nv_bfloat16* xb = reinterpret_cast<const __nv_bfloat16*>(&raw);
-  float x[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) x[i] = __bfloat162float(xb[i]);
-
-  // fp32 mean of squares over the 128 dims of this head.
-  float ss = __fadd_rn(__fadd_rn(__fmul_rn(x[0], x[0]), __fmul_rn(x[1], x[1])),
-                       __fadd_rn(__fmul_rn(x[2], x[2]), __fmul_rn(x[3], x[3])));
-#pragma unroll
-  for (int off = 16; off >= 1; off >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, off));
-  const float inv = rsqrtf(__fadd_rn(__fmul_rn(ss, 1.0f / kHeadDim), a.eps));
-
-  const __nv_bfloat16* w = (is_q ? a.q_weight : a.k_weight) + d0;
-  float z[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float y = bf16_round(__fmul_rn(x[i], inv));            // (x32 * rsqrt).to(bf16)
-    z[i] = bf16_round(__fmul_rn(__bfloat162float(w[i]), y));     // weight * y, in bf16
-  }
-
-  // RoPE: dim d pairs with d +/- 64, i.e. lane +/- 16.
   long long pos_row = t;
   if (a.positions != nullptr) {
     pos_row = a.positions[t];
@@ -116,30 +111,54 @@ __global__ void __launch_bounds__(kWarps * 32)
   const float4 s4 = *reinterpret_cast<const float4*>(a.sin + pos_row * a.cs_row_stride + d0);
   const float cv[4] = {bf16_round(c4.x), bf16_round(c4.y), bf16_round(c4.z), bf16_round(c4.w)};
   const float sv[4] = {bf16_round(s4.x), bf16_round(s4.y), bf16_round(s4.z), bf16_round(s4.w)};
-
-  __nv_bfloat16 outv[4];
+  const __nv_bfloat16* wp = (is_q ? a.q_weight : a.k_weight) + d0;
+  float wv[4];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float partner = __shfl_xor_sync(0xffffffffu, z[i], 16);
-    const float rot = lane < 16 ? -partner : partner;  // rotate_half: [-x2, x1]
-    const float p1 = bf16_round(__fmul_rn(z[i], cv[i]));
-    const float p2 = bf16_round(__fmul_rn(rot, sv[i]));
-    outv[i] = __float2bfloat16_rn(__fadd_rn(p1, p2));
-  }
-  const uint2 packed = *reinterpret_cast<const uint2*>(outv);
+  for (int i = 0; i < 4; ++i) wv[i] = __bfloat162float(wp[i]);
 
-  if (is_q) {
-    *reinterpret_cast<uint2*>(a.q_out + t * a.q_out_row_stride + hr * kHeadDim + d0) = packed;
-    return;
+  // fp32 mean of squares per head (8 independent warp reductions, interleaved).
+  float x[kRowsPerWarp][4], ss[kRowsPerWarp];
+#pragma unroll
+  for (int r = 0; r < kRowsPerWarp; ++r) {
+    const __nv_bfloat16* xb = reinterpret_cast<const __nv_bfloat16*>(&raw[r]);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) x[r][i] = __bfloat162float(xb[i]);
+    ss[r] = __fadd_rn(__fadd_rn(__fmul_rn(x[r][0], x[r][0]), __fmul_rn(x[r][1], x[r][1])),
+                      __fadd_rn(__fmul_rn(x[r][2], x[r][2]), __fmul_rn(x[r][3], x[r][3])));
   }
-  const long long slot = a.slots[t];
-  if (slot < 0 || slot >= a.num_slots) {
-    if (lane == 0) atomicOr(status, kErrSlot);
-    return;
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) {
+#pragma unroll
+    for (int r = 0; r < kRowsPerWarp; ++r)
+      ss[r] = __fadd_rn(ss[r], __shfl_xor_sync(0xffffffffu, ss[r], off));
   }
-  __nv_bfloat16* dst =
-      a.k_pool + pool_offset(slot, hr - a.num_heads, d0, a.block_stride, a.head_stride);
-  *reinterpret_cast<uint2*>(dst) = packed;
+
+#pragma unroll
+  for (int r = 0; r < kRowsPerWarp; ++r) {
+    const float inv = rsqrtf(__fadd_rn(__fmul_rn(ss[r], 1.0f / kHeadDim), a.eps));
+    float z[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float y = bf16_round(__fmul_rn(x[r][i], inv));  // (x32 * rsqrt).to(bf16)
+      z[i] = bf16_round(__fmul_rn(wv[i], y));              // weight * y, in bf16
+    }
+    __nv_bfloat16 outv[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float partner = __shfl_xor_sync(0xffffffffu, z[i], 16);
+      const float rot = lane < 16 ? -partner : partner;  // rotate_half: [-x2, x1]
+      const float p1 = bf16_round(__fmul_rn(z[i], cv[i]));
+      const float p2 = bf16_round(__fmul_rn(rot, sv[i]));
+      outv[i] = __float2bfloat16_rn(__fadd_rn(p1, p2));
+    }
+    const uint2 packed = *reinterpret_cast<const uint2*>(outv);
+    if (is_q) {
+      *reinterpret_cast<uint2*>(a.q_out + t * a.q_out_row_stride + (row0 + r) * kHeadDim + d0) = packed;
+    } else {
+      *reinterpret_cast<uint2*>(a.k_pool + pool_offset(slot, row0 + r - a.num_heads, d0,
+                                                       a.block_stride, a.head_stride)) = packed;
+    }
+  }
 }
 
 struct ScatterArgs {

@@ -30,7 +30,7 @@ namespace {
 constexpr int kRec = 8;
 constexpr int kDecodeMaxTokens = 8;  // backends.py:32 SHORT_QUERY: the batched (short) path
 constexpr int kTileTokens = 64;      // query tokens per tile-mode work item (128 rows)
-constexpr int kItemsPerSm = 4;       // automatic split size aims at this many items per SM
+constexpr int kItemsPerSm = 1;       // automatic split: about one item per SM per KV head
 constexpr int kMinSplitPages = 32;   // a split streams at least 256 KiB per KV head
 constexpr int kTcBlockPages = 8;     // 128-key blocks of the tensor-core kernel
 constexpr int kTcMinSplitPages = 32; // tensor-core items cover at least 4 blocks

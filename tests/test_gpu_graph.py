@@ -1,0 +1,65 @@
+"""CUDA-graph capture of a whole decode step (28 layers of kernel A + attention).
+
+The C-ABI calls neither allocate nor synchronise, so once the first (eager) call on a device has
+set kernel attributes, built the pool's tensor maps and allocated the step's workspace, the step
+can be captured and replayed.  Replays must equal eager execution bit for bit, including after new
+inputs are copied into the captured buffers.
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from miniserve_b200.attention import attend, build_attention_metadata
+from miniserve_b200.kv_pool import allocate_kv_cache
+from miniserve_b200.qwen3_attention import qk_norm_rope_scatter
+from miniserve_b200.workloads import config2, rope_tables
+
+pytestmark = pytest.mark.gpu
+
+
+def test_graph_replay_matches_eager(cuda_device: torch.device) -> None:
+    dev = cuda_device
+    layers = 28
+    batch = config2(seed=5, num_seqs=32)
+    t = batch.num_tokens
+    g = torch.Generator(device=dev).manual_seed(5)
+    pool, views = allocate_kv_cache(layers, batch.num_blocks, 8, dev, zero=False)
+    pool.normal_(generator=g)
+    pool_copy = pool.clone()
+    qkv = torch.randn(layers, t, 4096, generator=g, device=dev, dtype=torch.bfloat16)
+    qw = (1 + 0.1 * torch.randn(layers, 128, generator=g, device=dev)).bfloat16()
+    kw = (1 + 0.1 * torch.randn(layers, 128, generator=g, device=dev)).bfloat16()
+    cos_t, sin_t = rope_tables(128, batch.max_position + 8, 1e6, dev)
+    pos = torch.from_numpy(batch.positions).to(dev)
+    slots = torch.from_numpy(batch.slots).to(dev)
+    cos, sin = cos_t[pos], sin_t[pos]
+    meta = build_attention_metadata(batch.chunks, slots, 16, pages_per_split=16)
+    assert meta.info.n_combine > 0
+    q_buf = torch.empty(t, 16, 128, dtype=torch.bfloat16, device=dev)
+    out = torch.empty(layers, t, 16, 128, dtype=torch.bfloat16, device=dev)
+
+    def step() -> None:
+        for i in range(layers):
+            kc, vc = views[i]
+            qk_norm_rope_scatter(qkv[i], qw[i], kw[i], 1e-6, cos, sin, slots, kc, vc, 16, q_out=q_buf)
+            attend(q_buf, kc, vc, meta, 128**-0.5, out=out[i])
+
+    step()  # eager warm-up on this device (attributes, tensor maps, workspace)
+    torch.cuda.synchronize(dev)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+
+    for trial in range(2):
+        new_qkv = torch.randn(layers, t, 4096, generator=g, device=dev, dtype=torch.bfloat16)
+        qkv.copy_(new_qkv)
+        pool.copy_(pool_copy)
+        graph.replay()
+        torch.cuda.synchronize(dev)
+        replayed = out.clone()
+        pool.copy_(pool_copy)
+        step()
+        torch.cuda.synchronize(dev)
+        assert torch.equal(replayed, out), trial
