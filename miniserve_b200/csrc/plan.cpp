@@ -7,8 +7,8 @@
 // its own block table (CSR), and the work is cut into (query tile, KV page range) items:
 //   * a sequence with <= 8 new tokens (decode, speculative verify) is one decode tile;
 //   * a chunk of 9..64 tokens is one tile for the mma.sync tile kernel;
-//   * a chunk of more than 64 tokens is cut into tiles of 64 query tokens for the tcgen05
-//     tensor-core kernel, whose page ranges are split in whole 128-key blocks (8 pages);
+//   * a chunk of more than 64 tokens is cut into items of 128 query tokens (two 128-row tiles)
+//     for the tcgen05 tensor-core kernel, whose page ranges are split in whole 128-key blocks;
 //   * a tile's visible pages, ceil((num_cached + tok0 + n_q) / 16), are split into near-equal
 //     ranges of at most `pages_per_split` pages; split tiles get partial rows in the workspace
 //     and a combine record.
@@ -29,7 +29,8 @@ namespace {
 
 constexpr int kRec = 8;
 constexpr int kDecodeMaxTokens = 8;  // backends.py:32 SHORT_QUERY: the batched (short) path
-constexpr int kTileTokens = 64;      // query tokens per tile-mode work item (128 rows)
+constexpr int kTileTokens = 64;      // longest chunk of the mma.sync tile kernel (128 rows)
+constexpr int kTcTokens = 128;       // query tokens per tensor-core work item (2 x 128 rows)
 constexpr int kItemsPerSm = 1;       // automatic split: about one item per SM per KV head
 constexpr int kMinSplitPages = 32;   // a split streams at least 256 KiB per KV head
 constexpr int kTcBlockPages = 8;     // 128-key blocks of the tensor-core kernel
@@ -107,7 +108,7 @@ extern "C" int ms_plan_build(int32_t num_seqs, const int32_t* flat_start, const 
                          " blocks but its table has " + std::to_string(tlen));
       return MS_ERR_PLAN;
     }
-    const int step = n <= kDecodeMaxTokens ? kDecodeMaxTokens : kTileTokens;
+    const int step = n <= kDecodeMaxTokens ? kDecodeMaxTokens : (n <= kTileTokens ? kTileTokens : kTcTokens);
     for (int64_t t0 = 0; t0 < n; t0 += step) {
       const int nq = static_cast<int>(std::min<int64_t>(step, n - t0));
       const int pages = static_cast<int>((c + t0 + nq + block_size - 1) / block_size);

@@ -43,14 +43,14 @@ def check_plan(chunks: list[SeqChunk], num_tokens: int, split: int = 0) -> None:
             elif kind == "til":
                 assert 8 < c.num_new <= 64 and tok0 == 0 and nq == c.num_new
             else:
-                assert c.num_new > 64 and tok0 % 64 == 0 and nq == min(64, c.num_new - tok0)
+                assert c.num_new > 64 and tok0 % 128 == 0 and nq == min(128, c.num_new - tok0)
                 assert pb % 8 == 0, "tensor-core ranges start on 128-key blocks"
             cover.setdefault((seq, tok0), []).append((pb, pe, part))
         lens = [int(it[4] - it[3]) for it in items]
         assert lens == sorted(lens, reverse=True), "items must be longest first"
     combos = {(int(r[0]), int(r[1])): r for r in comb}
     for c_idx, c in enumerate(chunks):
-        step = 8 if c.num_new <= 8 else 64
+        step = 8 if c.num_new <= 8 else (64 if c.num_new <= 64 else 128)
         for tok0 in range(0, c.num_new, step):
             nq = min(step, c.num_new - tok0)
             pages = -(-(c.num_cached + tok0 + nq) // 16)
