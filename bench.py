@@ -54,9 +54,11 @@ def parse() -> argparse.Namespace:
                    help="time eager launches instead of replaying the captured step")
     p.add_argument("--layers", type=int, default=LAYERS,
                    help="layers per step (28 for the headline; fewer only for small profiles)")
-    p.add_argument("--workload", choices=["cfg2", "cfg3", "cfg4"], default="cfg2",
-                   help="cfg2 is the headline; cfg3 (mixed prefill) and cfg4 (prefix + verify) "
-                        "are reported alongside")
+    p.add_argument("--workload", choices=["cfg2", "cfg3", "cfg4", "cfg5"], default="cfg2",
+                   help="cfg2 is the headline; cfg3 (mixed prefill), cfg4 (prefix + verify) and "
+                        "cfg5 (box scale: 8192 rows sharded over the ranks) are reported alongside")
+    p.add_argument("--pool-gb", type=float, default=150.0,
+                   help="cfg5: per-GPU pool shared by all layers")
     return p.parse_args()
 
 
@@ -135,7 +137,9 @@ def attention_bytes(batch) -> tuple[int, int, int]:
     entries.  Kernel A: the qkv row read, q written, K and V written to the pool, cos/sin rows and
     the slot/position indices.  FLOPs: 4 * 128 * 16 heads per (query token, visible key).
     """
-    kv_tokens = batch.unique_kv_tokens()
+    # A pool shared by all layers (config 5) still streams every context token from HBM, since
+    # the pool is far larger than L2: count the logical tokens there.
+    kv_tokens = batch.kv_tokens_read() if getattr(batch, "aliased", False) else batch.unique_kv_tokens()
     t = batch.num_tokens
     tables = sum(-(-c.context_len // 16) for c in batch.chunks)
     attn = kv_tokens * KVH * D * 2 * 2 + t * H * D * 2 * 2 + tables * 4
@@ -149,20 +153,27 @@ def run_ours(args: argparse.Namespace, rank: int, world: int, device: torch.devi
     from miniserve_b200.attention import attend, build_attention_metadata
     from miniserve_b200.kv_pool import allocate_kv_cache
     from miniserve_b200.qwen3_attention import qk_norm_rope_scatter
-    from miniserve_b200.workloads import config2, config3, config4, rope_tables
+    from miniserve_b200.workloads import config2, config3, config4, config5, rope_tables
 
+    alias_layers = False
     if args.workload == "cfg2":
         batch = config2(seed=1000 + rank, num_seqs=args.seqs)
     elif args.workload == "cfg3":
         batch = config3(seed=1000 + rank)
-    else:
+    elif args.workload == "cfg4":
         batch = config4(seed=1000 + rank)
+    else:
+        batch = config5(rank, world, seed=0, pool_bytes=args.pool_gb * 1e9)
+        alias_layers = True  # one pool shared by all layers (it cannot hold 28 separate ones)
     LAYERS = args.layers
     t = batch.num_tokens
     g = torch.Generator(device=device).manual_seed(1234 + rank)
-    pool, views = allocate_kv_cache(LAYERS, batch.num_blocks, KVH, device, zero=False)
-    for layer in range(LAYERS):
+    pool, views = allocate_kv_cache(1 if alias_layers else LAYERS, batch.num_blocks, KVH, device,
+                                    zero=False)
+    for layer in range(pool.shape[0]):
         pool[layer].normal_(generator=g)
+    if alias_layers:
+        views = views * LAYERS
     qkv_all = torch.randn(LAYERS, t, (H + 2 * KVH) * D, generator=g, device=device,
                           dtype=torch.bfloat16)
     qw = (1 + 0.1 * torch.randn(LAYERS, D, generator=g, device=device)).bfloat16()
@@ -291,7 +302,9 @@ def run_ours(args: argparse.Namespace, rank: int, world: int, device: torch.devi
         "logical_kv_tokens": batch.kv_tokens_read(),
         "kernel_a_bytes": a_bytes,
         "tokens": t,
-        "kv_tokens": batch.unique_kv_tokens(),
+        "kv_tokens": (batch.kv_tokens_read() if getattr(batch, "aliased", False)
+                      else batch.unique_kv_tokens()),
+        "pool_shared_by_layers": alias_layers,
         "num_blocks": batch.num_blocks,
         "clocks": clocks,
         "launches_per_step": LAYERS * launches_per_layer,
@@ -382,7 +395,7 @@ def main() -> None:
             "warmup": args.warmup,
             "ms_per_step": t_layer * LAYERS * 1e3,
             "higher_is_better": True,
-            "scaling": "weak",
+            "scaling": "strong" if args.workload == "cfg5" else "weak",
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic",
@@ -417,12 +430,14 @@ def main() -> None:
     r = run_ours(args, rank, world, device)
     ms = torch.tensor([r["total_ms"], r["e2e_ms"], r["attn_ms"], r["eager_ms"]],
                       dtype=torch.float64, device=device)
+    toks = torch.tensor([r["tokens"]], dtype=torch.float64, device=device)
     if world > 1:
         torch.distributed.all_reduce(ms, op=torch.distributed.ReduceOp.MAX)
+        torch.distributed.all_reduce(toks, op=torch.distributed.ReduceOp.SUM)
     total_ms, e2e_ms, attn_ms, eager_ms = (float(x) for x in ms.cpu())
     ms_per_step = total_ms / args.steps
     e2e_per_step = e2e_ms / args.steps
-    tokens_all = r["tokens"] * world
+    tokens_all = int(toks.item())
 
     cpu = None
     if (rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload == "cfg2"
@@ -457,7 +472,10 @@ def main() -> None:
             "config": {
                 "workload": (f"config2: {args.seqs} decode seqs/GPU, ctx U[256,4096], 16q/8kv "
                              f"heads, d128, block 16, {args.layers} layers"
-                             if args.workload == "cfg2" else args.workload),
+                             if args.workload == "cfg2" else
+                             "config5: 8192 decode seqs in total, ctx logU[512,32768], sharded by "
+                             f"tokens over {world} GPU(s), one {args.pool_gb:.0f} GB pool per GPU "
+                             "shared by the 28 layers" if args.workload == "cfg5" else args.workload),
                 "layers": args.layers,
                 "kv_tokens_per_layer": r["kv_tokens"],
                 "logical_kv_tokens_per_layer": r["logical_kv_tokens"],

@@ -35,6 +35,10 @@ constexpr int kItemsPerSm = 1;       // automatic split: about one item per SM p
 constexpr int kMinSplitPages = 32;   // a split streams at least 256 KiB per KV head
 constexpr int kTcBlockPages = 8;     // 128-key blocks of the tensor-core kernel
 constexpr int kTcMinSplitPages = 32; // tensor-core items cover at least 4 blocks
+// Splitting a tensor-core item's keys costs a combine over 256 partial rows, which only pays when
+// the items alone cannot occupy the GPU: with at least this many items per 16 SMs (x 8 KV heads,
+// i.e. half the SMs busy), they are not split.
+constexpr int kTcNoSplitItemsPer16Sms = 1;
 
 struct Item {
   int seq, tok0, n_q, pb, pe, part_row;
@@ -129,7 +133,11 @@ extern "C" int ms_plan_build(int32_t num_seqs, const int32_t* flat_start, const 
 
   std::vector<Item> dec, til, tcv, comb;
   int64_t part_rows = 0;
-  const int tc_split = std::max(kTcMinSplitPages, (split + kTcBlockPages - 1) / kTcBlockPages * kTcBlockPages);
+  int64_t n_tc_tiles = 0;
+  for (const Item& t : tiles) n_tc_tiles += num_new[t.seq] > kTileTokens ? 1 : 0;
+  int tc_split = std::max(kTcMinSplitPages, (split + kTcBlockPages - 1) / kTcBlockPages * kTcBlockPages);
+  if (pages_per_split == 0 && n_tc_tiles * 16 >= static_cast<int64_t>(num_sms) * kTcNoSplitItemsPer16Sms)
+    tc_split = 1 << 30;
   for (const Item& t : tiles) {
     const int pages = t.pe;
     const int nn = num_new[t.seq];

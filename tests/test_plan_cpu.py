@@ -111,3 +111,21 @@ def test_plan_rejects_rows_outside_batch() -> None:
 def test_plan_rejects_other_block_sizes() -> None:
     with pytest.raises(ValueError, match="block_size"):
         plan_batch([SeqChunk(0, 1, 0, [0])], 1, block_size=32)
+
+
+@pytest.mark.parametrize("world", [1, 8])
+def test_config5_shard_plans(world: int) -> None:
+    from miniserve_b200.workloads import config5, config5_contexts
+
+    ctx = config5_contexts(seed=0)
+    total_rows = 0
+    for rank in sorted({0, world - 1}):
+        b = config5(rank, world, seed=0, pool_bytes=20e9)
+        assert all(0 <= x < b.num_blocks for c in b.chunks[:50] for x in c.block_table)
+        assert all(len(c.block_table) * 16 >= c.context_len for c in b.chunks)
+        total_rows += len(b.chunks)
+        if world == 1:
+            assert len(b.chunks) == len(ctx) and b.aliased
+    packed, info = plan_batch(config5(0, world, seed=0, pool_bytes=20e9).chunks,
+                              len(config5(0, world, seed=0, pool_bytes=20e9).chunks), 16, 148, 0)
+    assert info.n_decode_items >= len(ctx) // world - 1
