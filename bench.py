@@ -54,9 +54,11 @@ def parse() -> argparse.Namespace:
                    help="time eager launches instead of replaying the captured step")
     p.add_argument("--layers", type=int, default=LAYERS,
                    help="layers per step (28 for the headline; fewer only for small profiles)")
-    p.add_argument("--workload", choices=["cfg2", "cfg3", "cfg4", "cfg5"], default="cfg2",
-                   help="cfg2 is the headline; cfg3 (mixed prefill), cfg4 (prefix + verify) and "
-                        "cfg5 (box scale: 8192 rows sharded over the ranks) are reported alongside")
+    p.add_argument("--workload", choices=["cfg1", "cfg2", "cfg3", "cfg4", "cfg5"],
+                   default="cfg2",
+                   help="cfg2 is the headline; cfg1 (8 short decode rows), cfg3 (mixed prefill), "
+                        "cfg4 (prefix + verify) and cfg5 (box scale: 8192 rows sharded over the "
+                        "ranks) are reported alongside")
     p.add_argument("--pool-gb", type=float, default=150.0,
                    help="cfg5: per-GPU pool shared by all layers")
     return p.parse_args()
@@ -153,10 +155,13 @@ def run_ours(args: argparse.Namespace, rank: int, world: int, device: torch.devi
     from miniserve_b200.attention import attend, build_attention_metadata
     from miniserve_b200.kv_pool import allocate_kv_cache
     from miniserve_b200.qwen3_attention import qk_norm_rope_scatter
-    from miniserve_b200.workloads import config2, config3, config4, config5, rope_tables
+    from miniserve_b200.workloads import (config1, config2, config3, config4, config5,
+                                          rope_tables)
 
     alias_layers = False
-    if args.workload == "cfg2":
+    if args.workload == "cfg1":
+        batch = config1(seed=1000 + rank)
+    elif args.workload == "cfg2":
         batch = config2(seed=1000 + rank, num_seqs=args.seqs)
     elif args.workload == "cfg3":
         batch = config3(seed=1000 + rank)
