@@ -77,6 +77,57 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   return false;
 }
 
+// Without a suspend-time hint: a hinted try_wait costs about 190 cycles even on a phase that has
+// already completed, a plain one about 46.  Threads that feed the tensor core (or sit on its
+// critical path) use this form; every cycle they stall is an idle tensor-core cycle.
+__device__ __forceinline__ bool mbar_try_wait_nohint(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// Bounded wait on the latency-critical path: the abort flag is read only while the phase is still
+// open (reading it costs a shared-memory round trip), never on the fast path.
+__device__ __forceinline__ bool mbar_wait_fast(uint64_t* bar, uint32_t parity,
+                                               const volatile int* abort_flag) {
+  for (int i = 0; i < kSpinLimit; ++i) {
+    if (mbar_try_wait_nohint(bar, parity)) return true;
+    if (*abort_flag) return false;
+  }
+  return false;
+}
+
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// Bounded wait for the thread that issues tcgen05.mma / tcgen05.commit.  A blocking try_wait
+// placed after a tcgen05.commit waits for that commit's arrive, i.e. for every MMA in flight
+// (about 370 idle tensor-core cycles per wait); the non-blocking test_wait does not.  The abort
+// flag is read once every 64 polls.
+__device__ __forceinline__ bool mbar_wait_mma(uint64_t* bar, uint32_t parity,
+                                              const volatile int* abort_flag) {
+  for (int i = 0; i < 16 * kSpinLimit; ++i) {
+    if (mbar_test_wait(bar, parity)) return true;
+    if ((i & 63) == 63 && *abort_flag) return false;
+  }
+  return false;
+}
+
 // ---- TMA (tensor) loads: plain CTA-local destination, no multicast ---------------------------
 
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {

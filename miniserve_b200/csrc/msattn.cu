@@ -49,7 +49,7 @@ struct MapKey {
   uintptr_t base;
   int num_blocks;
   int num_kv;
-  int box;  // 0: whole (block, head) page pair; 1: one 2 KiB quarter (K lo/hi, V lo/hi)
+  int box;  // 0: whole (block, head) page pair; 1: one 2 KiB quarter; 2: two quarters (4 KiB)
   bool operator==(const MapKey& o) const {
     return device == o.device && base == o.base && num_blocks == o.num_blocks &&
            num_kv == o.num_kv && box == o.box;
@@ -68,8 +68,9 @@ static std::unordered_map<MapKey, CUtensorMap, MapKeyHash> g_maps;
 
 // One layer's pool region viewed as a 5-D tensor {64 dims, 16 tokens, 4 quarters (K lo, K hi,
 // V lo, V hi), KV heads, blocks}.  Box kind 0 is a whole 8 KiB (block, head) page pair (decode
-// kernel); box kind 1 is one 2 KiB quarter, so the tensor-core kernel can lay 8 pages' K and V
-// out as contiguous 128-key operand tiles.
+// kernel); box kind 1 is one 2 KiB quarter, so the tensor-core kernel can lay 8 pages' K out as a
+// contiguous 128-key operand tile; box kind 2 is two quarters (a page's whole V, 4 KiB), which the
+// tensor-core kernel reads as an MN-major operand one page per 16-key step.
 static int kv_tensor_map(const void* k_cache, int num_blocks, int num_kv, int box_kind,
                          CUtensorMap* out) {
   int dev = 0;
@@ -91,7 +92,7 @@ static int kv_tensor_map(const void* k_cache, int num_blocks, int num_kv, int bo
                               static_cast<cuuint64_t>(num_blocks)};
   const cuuint64_t strides[4] = {128, 2048, ms::kPageKVBytes,
                                  static_cast<cuuint64_t>(num_kv) * ms::kPageKVBytes};
-  const cuuint32_t box[5] = {64, 16, box_kind == 0 ? 4u : 1u, 1, 1};
+  const cuuint32_t box[5] = {64, 16, box_kind == 0 ? 4u : (box_kind == 1 ? 1u : 2u), 1, 1};
   const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
   CUtensorMap map;
   const CUresult r = fn(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, const_cast<void*>(k_cache), dims,
@@ -360,9 +361,11 @@ extern "C" int ms_paged_attention(const void* q, int64_t q_row_stride, void* out
   CUtensorMap map;
   rc = kv_tensor_map(k_cache, num_blocks, num_kv_heads, 0, &map);
   if (rc) return rc;
-  CUtensorMap qmap;
+  CUtensorMap kmap, vmap;
   if (plan->n_tc_items > 0) {
-    rc = kv_tensor_map(k_cache, num_blocks, num_kv_heads, 1, &qmap);
+    rc = kv_tensor_map(k_cache, num_blocks, num_kv_heads, 1, &kmap);
+    if (rc) return rc;
+    rc = kv_tensor_map(k_cache, num_blocks, num_kv_heads, 2, &vmap);
     if (rc) return rc;
   }
 
@@ -393,7 +396,7 @@ extern "C" int ms_paged_attention(const void* q, int64_t q_row_stride, void* out
     a.items = plan_dev + plan->off_tc;
     a.n_items = plan->n_tc_items;
     ms::prefill_tc_kernel<<<plan->n_tc_items * num_kv_heads, ms::TcCfg::kThreads,
-                            ms::TcCfg::kSmemBytes, s>>>(qmap, a);
+                            ms::TcCfg::kSmemBytes, s>>>(kmap, vmap, a);
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail("prefill_tc launch", e);
   }

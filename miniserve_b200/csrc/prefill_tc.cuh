@@ -7,25 +7,32 @@
 // range of the sequence's KV pages, walked in blocks of 128 keys.
 //
 //   warps 0-3   softmax for tile A, warps 4-7 softmax for tile B: one thread per row (TMEM lane).
-//               Per block: read S from TMEM, causal / range mask (cached length as offset), row
-//               max, p = 2^(s*scale*log2e - m) (a quarter of them on the FMA pipe), row sum, and P
-//               written back as bf16 into the S columns it came from (tcgen05.st).  The running
-//               max only moves (and O in TMEM is rescaled) when it grows by more than 2^8.
-//   warps 8, 10 TMA producers for K and for V: per 128-key block, 16 boxes of 2 KiB (8 pages x
-//               two 64-dim halves, one box per lane) into a 2-stage K ring and a 3-stage V ring;
-//               pages past the item's range are read from an out-of-range block id, which the
-//               TMA unit fills with zeros.  Separate warps keep K_{j+1} from queueing behind V_j.
-//   warp 9      TMEM allocator (512 columns) and, on one thread, the MMA issuer:
-//                 S_t(j) = Q_t K_j^T   (M=128, N=128, K=128, A and B from shared memory)
-//                 O_t   += P_t(j) V_j  (M=128, N=128, K=128, A = P from TMEM, B from shared memory)
-//               in the order S_A(0) S_B(0) | O_A += P_A(0) V_0, S_A(1) | O_B += P_B(0) V_0, S_B(1) |
-//               ... so the tensor core works on one tile while the other tile's softmax runs.
-//               MMAs execute in issue order, so S_t(j+1) overwrites P_t(j) only after it was read.
+//               Per block: load the row's 128 scores from TMEM into registers and release the S
+//               columns at once (the next S of this tile can start), causal / range mask (cached
+//               length as offset), row max, p = 2^(s*scale*log2e - m) (3 of 8 pairs on the FMA
+//               pipe), row sum, and P packed to bf16 in registers; then, once this tile's previous
+//               P*V has finished with its P buffer in shared memory, P is stored there.  The
+//               running max only moves (and O in TMEM is rescaled) when it grows by more than 2^8.
+//   warp 8      TMA producer: K and V blocks in consumption order K_0, K_1, V_0, K_2, V_1, ... into
+//               a 3-slot ring of 32 KiB.  K: 16 boxes of 2 KiB (8 pages x two 64-dim halves), laid
+//               out as [half][128 keys][64] for the K-major operand; V: 8 boxes of 4 KiB (one page
+//               each), read as an MN-major operand one page per 16-key step.  One box per lane;
+//               pages past the item's range are read from an out-of-range block id, which the TMA
+//               unit fills with zeros.
+//   warp 9      TMEM allocator (512 columns) and, on one thread, the MMA issuer; every MMA takes
+//               both operands from shared memory (an operand in TMEM runs at half rate):
+//                 S_t(j+1) = Q_t K_{j+1}^T  (M=128, N=128, K=128) as soon as S_t(j) is in registers
+//                 O_t     += P_t(j) V_j     (M=128, N=128, K=128) as soon as P_t(j) is stored
+//               in the order S_A(j+1) S_B(j+1) O_A(j) O_B(j), so the scores of the next block are
+//               ready before the softmax needs them and the tensor core never waits for a P store
+//               of the same block.  P in shared memory, not TMEM: tcgen05.st traffic slows the
+//               tensor core, plain shared-memory stores do not.
 //
-// TMEM columns: [0,128) S_A / P_A, [128,256) S_B / P_B, [256,384) O_A, [384,512) O_B.
-// Operands in shared memory are 128-byte swizzled with 8-row atoms 1024 bytes apart: Q and K
-// K-major, V MN-major.  Every wait is bounded; on a timeout the CTA records kErrTimeout, stops,
-// lets issued MMAs and TMA copies finish, frees TMEM and exits.
+// TMEM columns: S_A at 0, S_B at 128, O_A at 256, O_B at 384.  Shared memory: Q_A, Q_B, P_A, P_B
+// (each [2 halves][128 rows][64] bf16, K-major) and the K/V ring, all 128-byte swizzled with
+// 8-row atoms 1024 bytes apart.  Every wait is
+// bounded; on a timeout the CTA records kErrTimeout, stops, lets issued MMAs and TMA copies
+// finish, frees TMEM and exits.
 #pragma once
 
 #include "paged_attention.cuh"
@@ -34,19 +41,19 @@
 namespace ms {
 
 struct TcCfg {
-  static constexpr int kThreads = 352;
-  static constexpr int kKStages = 2;
-  static constexpr int kVStages = 3;
-  static constexpr int kTileTokens = 64;   // query tokens per 128-row tile
-  static constexpr int kItemTokens = 128;  // query tokens per work item (two tiles)
+  static constexpr int kThreads = 320;
+  static constexpr int kSlots = 3;          // K/V ring slots (one 128-key K or V block each)
+  static constexpr int kTileTokens = 64;    // query tokens per 128-row tile
+  static constexpr int kItemTokens = 128;   // query tokens per work item (two tiles)
   static constexpr int kBlockKeys = 128;
   static constexpr int kQBytes = 32768;     // one tile: [2 halves][128 rows][64]
-  static constexpr int kTileBytes = 32768;  // one 128-key K (or V) block
-  static constexpr int kQOff = 0;                              // Q_A, Q_B
-  static constexpr int kKOff = 2 * kQBytes;                    // K ring
-  static constexpr int kVOff = kKOff + kKStages * kTileBytes;  // V ring
-  static constexpr int kBarOff = kVOff + kVStages * kTileBytes;
-  static constexpr int kSmemBytes = 1024 + kBarOff + 24 * 8;
+  static constexpr int kSlotBytes = 32768;  // one 128-key K (or V) block
+  static constexpr int kQOff = 0;                          // Q_A, Q_B
+  static constexpr int kPOff = 2 * kQBytes;                // P_A, P_B
+  static constexpr int kRingOff = kPOff + 2 * kQBytes;     // K/V ring
+  static constexpr int kBarOff = kRingOff + kSlots * kSlotBytes;
+  static constexpr int kNumBars = 2 * kSlots + 2 + 2 + 2 + 2 + 1;
+  static constexpr int kSmemBytes = 1024 + kBarOff + (kNumBars + 2) * 8;
   static_assert(kSmemBytes <= 232448, "shared memory budget");
   static constexpr uint32_t kTmemCols = 512;
   static constexpr uint32_t kOCol = 256;
@@ -92,101 +99,81 @@ __device__ __forceinline__ float2 exp2_fma2(float2 x) {
                      __int_as_float(__float_as_int(p.y) + (ny << 23)));
 }
 
-// The row max of one block's 128 raw scores (masked ones excluded), read from TMEM in 32-column
-// chunks with the next chunk's load in flight while the current one is reduced (tcgen05.wait::ld
-// waits for every load issued before it, so the buffers alternate).
-__device__ __forceinline__ float softmax_max_pass(uint32_t s_addr, bool need_mask, int k0, int qpos,
-                                                  int key_end) {
-  float buf[2][32];
+__device__ __forceinline__ void mask_scores32(float (&v)[32], int k0, int qpos, int key_end) {
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    const int kp = k0 + i;
+    if (kp > qpos || kp >= key_end) v[i] = -INFINITY;
+  }
+}
+
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
+                                             uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c),
+               "r"(d)
+               : "memory");
+}
+
+// Forces the 16 words to be computed before any later volatile asm (such as a TMEM load), so
+// the compiler cannot keep their inputs alive across it.
+__device__ __forceinline__ void pin16(const uint32_t (&v)[16]) {
+  asm volatile("" ::"r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]),
+               "r"(v[7]), "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]),
+               "r"(v[14]), "r"(v[15]));
+}
+
+__device__ __forceinline__ float max128(const float (&s0)[32], const float (&s1)[32],
+                                        const float (&s2)[32], const float (&s3)[32]) {
   float mxa[8];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) mxa[i] = -INFINITY;
-  tmem_ld32(s_addr, buf[0]);
-  tmem_wait_ld();
+  for (int i = 0; i < 8; ++i) mxa[i] = fmaxf(fmaxf(s0[i], s1[i]), fmaxf(s2[i], s3[i]));
 #pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    if (c + 1 < 4) tmem_ld32(s_addr + (c + 1) * 32, buf[(c + 1) & 1]);
-    float* sv = buf[c & 1];
-    if (need_mask) {
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const int kp = k0 + c * 32 + i;
-        if (kp > qpos || kp >= key_end) sv[i] = -INFINITY;
-      }
-    }
-#pragma unroll
-    for (int i = 0; i < 32; ++i) mxa[i & 7] = fmaxf(mxa[i & 7], sv[i]);
-    if (c + 1 < 4) tmem_wait_ld();
-  }
+  for (int i = 8; i < 32; ++i)
+    mxa[i & 7] = fmaxf(mxa[i & 7], fmaxf(fmaxf(s0[i], s1[i]), fmaxf(s2[i], s3[i])));
   return fmaxf(fmaxf(fmaxf(mxa[0], mxa[1]), fmaxf(mxa[2], mxa[3])),
                fmaxf(fmaxf(mxa[4], mxa[5]), fmaxf(mxa[6], mxa[7])));
 }
 
-// The exponential pass for one row: p = 2^(s * scale_log2 - m) for the 128 scores, read back from
-// TMEM with the next chunk's load in flight, the row sum, and P as packed bf16 pairs stored into the
-// first 64 columns of the same TMEM region as each chunk finishes (chunk c's 16 columns overwrite
-// scores of chunks <= c, already consumed).  Elements are processed in pairs with the paired fp32
-// instructions.  kMasked: apply the causal / range mask and use the MUFU for every exponential
-// (ex2(-inf) = 0); otherwise 3 of every 8 pairs go to the FMA pipe (exp2_fma2), which balances the
-// MUFU pipe against instruction issue when two softmax warps share a sub-partition.  The two forms
-// are separate instantiations: choosing per element at run time doubles the cost of the loop.
+// p = 2^(s * scale_log2 - m) for 32 scores, accumulated into the pair sums and packed as 16 bf16
+// pairs.  Elements are processed in pairs with the paired fp32 instructions.  kMasked: the block
+// holds masked (-inf) scores, so every exponential goes to the MUFU (ex2(-inf) = 0); otherwise 3 of
+// every 8 pairs go to the FMA pipe (exp2_fma2), which balances the MUFU pipe against instruction
+// issue when two softmax warps share a sub-partition.  The two forms are separate instantiations:
+// choosing per element at run time doubles the cost of the loop.
 template <bool kMasked>
-__device__ __forceinline__ float softmax_exp_pass(uint32_t s_addr, float scale_log2, float neg_mu,
-                                                  int k0, int qpos, int key_end) {
-  float buf[2][32];
-  float2 suma[4];
+__device__ __forceinline__ void exp_pack32(const float (&sv)[32], float2 sc2, float2 nm2,
+                                           float2 (&suma)[4], uint32_t (&packed)[16]) {
 #pragma unroll
-  for (int i = 0; i < 4; ++i) suma[i] = make_float2(0.f, 0.f);
-  const float2 sc2 = make_float2(scale_log2, scale_log2);
-  const float2 nm2 = make_float2(neg_mu, neg_mu);
-  tmem_ld32(s_addr, buf[0]);
-  tmem_wait_ld();
-#pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    if (c + 1 < 4) tmem_ld32(s_addr + (c + 1) * 32, buf[(c + 1) & 1]);
-    const float* sv = buf[c & 1];
-    uint32_t packed[16];
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      float2 x = __ffma2_rn(make_float2(sv[2 * i], sv[2 * i + 1]), sc2, nm2);
-      float2 p;
-      if constexpr (kMasked) {
-        const int kp = k0 + c * 32 + 2 * i;
-        if (kp > qpos || kp >= key_end) x.x = -INFINITY;
-        if (kp + 1 > qpos || kp + 1 >= key_end) x.y = -INFINITY;
-        p = make_float2(fast_exp2(x.x), fast_exp2(x.y));
-      } else {
-        p = (i & 7) < 3 ? exp2_fma2(x) : make_float2(fast_exp2(x.x), fast_exp2(x.y));
-      }
-      suma[i & 3] = __fadd2_rn(suma[i & 3], p);
-      packed[i] = pack_bf16(p.x, p.y);
+  for (int i = 0; i < 16; ++i) {
+    const float2 x = __ffma2_rn(make_float2(sv[2 * i], sv[2 * i + 1]), sc2, nm2);
+    float2 p;
+    if constexpr (kMasked) {
+      p = make_float2(fast_exp2(x.x), fast_exp2(x.y));
+    } else {
+      p = (i & 7) < 3 ? exp2_fma2(x) : make_float2(fast_exp2(x.x), fast_exp2(x.y));
     }
-    tmem_st16(s_addr + c * 16, packed);
-    if (c + 1 < 4) tmem_wait_ld();
+    suma[i & 3] = __fadd2_rn(suma[i & 3], p);
+    packed[i] = pack_bf16(p.x, p.y);
   }
-  tmem_wait_st();
-  const float2 s01 = __fadd2_rn(suma[0], suma[1]);
-  const float2 s23 = __fadd2_rn(suma[2], suma[3]);
-  const float2 st = __fadd2_rn(s01, s23);
-  return st.x + st.y;
 }
 
 __global__ void __launch_bounds__(TcCfg::kThreads, 1)
-    prefill_tc_kernel(const __grid_constant__ CUtensorMap page_map, const AttnArgs a) {
+    prefill_tc_kernel(const __grid_constant__ CUtensorMap k_map,
+                      const __grid_constant__ CUtensorMap v_map, const AttnArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  constexpr int NS = TcCfg::kSlots;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + TcCfg::kBarOff);
-  uint64_t* k_full = bars + 0;    // [kKStages]
-  uint64_t* k_empty = bars + 2;   // [kKStages]
-  uint64_t* v_full = bars + 4;    // [kVStages]
-  uint64_t* v_empty = bars + 7;   // [kVStages]
-  uint64_t* s_full = bars + 10;   // [2 tiles]
-  uint64_t* p_full = bars + 12;   // [2 tiles]
-  uint64_t* o_ready = bars + 14;  // [2 tiles]
-  uint64_t* mma_drain = bars + 16;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 17);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 18);
+  uint64_t* slot_full = bars;              // [NS]
+  uint64_t* slot_empty = slot_full + NS;   // [NS]
+  uint64_t* s_full = slot_empty + NS;      // [tile]: S_t(j) computed
+  uint64_t* s_free = s_full + 2;           // [tile]: S_t(j) read into registers
+  uint64_t* p_full = s_free + 2;           // [tile]: P_t(j) stored (and O_t rescaled)
+  uint64_t* pv_done = p_full + 2;          // [tile]: O_t += P_t(j) V_j finished
+  uint64_t* mma_drain = pv_done + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + TcCfg::kNumBars);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + TcCfg::kNumBars + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -201,7 +188,7 @@ __global__ void __launch_bounds__(TcCfg::kThreads, 1)
   const int key_lo = page_begin * kBlockTokens;
   const int key_end = page_end * kBlockTokens;
   // Blocks each tile sees inside this item's page range (a tile's last visible key is
-  // num_cached + tok0 + its last token).
+  // num_cached + tok0 + its last token).  Tile A never sees more blocks than tile B.
   int nblk_t[2];
 #pragma unroll
   for (int t = 0; t < 2; ++t) {
@@ -212,20 +199,20 @@ __global__ void __launch_bounds__(TcCfg::kThreads, 1)
                     : (vis_end - key_lo + TcCfg::kBlockKeys - 1) / TcCfg::kBlockKeys;
   }
   const int nblk = max(nblk_t[0], nblk_t[1]);
+  // Ring positions: K_0 first, then K_{j+1} (if any) and V_j for j = 0, 1, ...
+  auto pos_k = [](int j) { return j == 0 ? 0 : 2 * j - 1; };
+  auto pos_v = [nblk](int j) { return j + 1 < nblk ? 2 * j + 2 : 2 * j + 1; };
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < TcCfg::kKStages; ++s) {
-      mbar_init(&k_full[s], 1);
-      mbar_init(&k_empty[s], 1);
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&slot_full[s], 1);
+      mbar_init(&slot_empty[s], 1);
     }
-    for (int s = 0; s < TcCfg::kVStages; ++s) {
-      mbar_init(&v_full[s], 1);
-      mbar_init(&v_empty[s], 1);
-    }
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(&s_full[s], 1);
-      mbar_init(&p_full[s], 128);
-      mbar_init(&o_ready[s], 1);
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&s_full[t], 1);
+      mbar_init(&s_free[t], 128);
+      mbar_init(&p_full[t], 128);
+      mbar_init(&pv_done[t], 1);
     }
     mbar_init(mma_drain, 1);
     *abort_flag = 0;
@@ -255,52 +242,61 @@ __global__ void __launch_bounds__(TcCfg::kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
 
-  if (warp == 8 || warp == 10) {
-    // ---------------- TMA producers: warp 8 loads K_0 K_1 ..., warp 10 loads V_0 V_1 ... -----
-    // K_j waits until every S that reads K_{j-kKStages} has finished with its slot, V_j until
-    // every O += P V_{j-kVStages}.  Lanes 0..15 issue one 2 KiB box each: page lane/2, half lane%2.
-    const bool is_v = warp == 10;
-    const int stages = is_v ? TcCfg::kVStages : TcCfg::kKStages;
-    uint64_t* fulls = is_v ? v_full : k_full;
-    uint64_t* empties = is_v ? v_empty : k_empty;
-    uint8_t* ring = smem + (is_v ? TcCfg::kVOff : TcCfg::kKOff);
+  if (warp == 8) {
+    // ---------------- TMA producer ----------------
+    // Position p goes to slot p % NS once every MMA that read position p - NS has finished.
+    // K: lanes 0..15 issue one 2 KiB box each (page lane / 2, 64-dim half lane % 2) into
+    // [half][128 keys][64]; V: lanes 0..7 issue one 4 KiB box each (page lane) into [page][half]
+    // [16 keys][64].
     const int* table = a.tables + table_off + page_begin;
+    int ids_j = (lane < 8 && lane < npages) ? table[lane] : -1;           // block j's pages
+    int ids_j1 = (lane < 8 && 8 + lane < npages) ? table[8 + lane] : -1;  // block j + 1's
     int issued = 0;
-    int next = -1;  // block ids of the next block's pages, loaded one block ahead (lanes 0..7)
-    if (lane < 8 && lane < npages) next = table[lane];
-    for (int j = 0; j < nblk; ++j) {
-      const int s = j % stages;
-      const int mine = next;
-      next = -1;
-      if (lane < 8 && (j + 1) * 8 + lane < npages) next = table[(j + 1) * 8 + lane];
-      if (!is_v && lane < 8 && j * 8 + lane < npages &&
-          static_cast<unsigned>(mine) >= static_cast<unsigned>(a.num_blocks))
-        atomicOr(&g_status_word, kErrBlock);
+    auto load = [&](int p, bool is_v, int ids, int j) -> bool {
+      const int s = p % NS;
       int ok = 1;
+      if (!is_v && lane < 8 && j * 8 + lane < npages &&
+          static_cast<unsigned>(ids) >= static_cast<unsigned>(a.num_blocks))
+        atomicOr(&g_status_word, kErrBlock);
       if (lane == 0) {
         if (*abort_flag) ok = 0;
-        if (ok && j >= stages && !mbar_wait(&empties[s], ((j / stages) - 1) & 1)) {
+        if (ok && p >= NS && !mbar_wait(&slot_empty[s], ((p / NS) - 1) & 1)) {
           atomicOr(&g_status_word, kErrTimeout);
           *abort_flag = 1;
           ok = 0;
         }
-        if (ok) mbar_arrive_expect_tx(&fulls[s], TcCfg::kTileBytes);
+        if (ok) mbar_arrive_expect_tx(&slot_full[s], TcCfg::kSlotBytes);
       }
       ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (!ok) break;
-      const int b = __shfl_sync(0xffffffffu, mine, (lane & 15) >> 1);
-      if (lane < 16) {
-        const int pg = lane >> 1, half = lane & 1;
-        tma_load_5d_plain(ring + s * TcCfg::kTileBytes + half * 16384 + pg * 2048, &page_map,
-                          &fulls[s], 0, 0, (is_v ? 2 : 0) + half, kvh, b);
+      if (!ok) return false;
+      uint8_t* slot = smem + TcCfg::kRingOff + s * TcCfg::kSlotBytes;
+      if (is_v) {
+        const int b = __shfl_sync(0xffffffffu, ids, lane & 7);
+        if (lane < 8) tma_load_5d_plain(slot + lane * kPageBytes, &v_map, &slot_full[s], 0, 0, 2, kvh, b);
+      } else {
+        const int b = __shfl_sync(0xffffffffu, ids, (lane & 15) >> 1);
+        if (lane < 16) {
+          const int pg = lane >> 1, half = lane & 1;
+          tma_load_5d_plain(slot + half * 16384 + pg * (kPageBytes / 2), &k_map, &slot_full[s], 0,
+                            0, half, kvh, b);
+        }
       }
       __syncwarp();
       ++issued;
+      return true;
+    };
+    if (nblk > 0 && load(pos_k(0), false, ids_j, 0)) {
+      for (int j = 0; j < nblk; ++j) {
+        if (j + 1 < nblk && !load(pos_k(j + 1), false, ids_j1, j + 1)) break;
+        if (!load(pos_v(j), true, ids_j, j)) break;
+        ids_j = ids_j1;
+        ids_j1 = (lane < 8 && (j + 2) * 8 + lane < npages) ? table[(j + 2) * 8 + lane] : -1;
+      }
     }
+    // No copy may still be landing when the CTA exits: wait for the last use of each slot.
     if (lane == 0) {
-      const int first = issued > stages ? issued - stages : 0;
-      for (int j = first; j < issued; ++j) {
-        if (!mbar_wait(&fulls[j % stages], (j / stages) & 1)) {
+      for (int p = issued > NS ? issued - NS : 0; p < issued; ++p) {
+        if (!mbar_wait(&slot_full[p % NS], (p / NS) & 1)) {
           atomicOr(&g_status_word, kErrTimeout);
           break;
         }
@@ -312,65 +308,73 @@ __global__ void __launch_bounds__(TcCfg::kThreads, 1)
       constexpr uint32_t kIdescS = umma_idesc_bf16(128, 128, false);
       constexpr uint32_t kIdescPV = umma_idesc_bf16(128, 128, true);
       const uint32_t q_base = smem_u32(smem + TcCfg::kQOff);
-      const uint32_t k0base = smem_u32(smem + TcCfg::kKOff);
-      const uint32_t v0base = smem_u32(smem + TcCfg::kVOff);
+      const uint32_t p_base = smem_u32(smem + TcCfg::kPOff);
+      const uint32_t ring = smem_u32(smem + TcCfg::kRingOff);
       bool ok = true;
-      auto wait_k = [&](int j) -> bool {
-        if (*abort_flag || !mbar_wait(&k_full[j % TcCfg::kKStages], (j / TcCfg::kKStages) & 1))
-          return false;
+      auto wait_slot = [&](int p) -> bool {
+        if (!mbar_wait_mma(&slot_full[p % NS], (p / NS) & 1, abort_flag)) return false;
         tc_fence_after();
         return true;
       };
+      // Descriptors are built once; operand offsets are added to their start-address field
+      // (shared-memory addresses >> 4 fit its 14 bits with room to spare).
+      const uint64_t dq = umma_smem_desc_sw128(q_base, 16, 1024);
+      const uint64_t dp = umma_smem_desc_sw128(p_base, 16, 1024);
+      const uint64_t dk = umma_smem_desc_sw128(ring, 16, 1024);
+      const uint64_t dv = umma_smem_desc_sw128(ring, 2048, 1024);  // [page][half][16 keys][64]
+      constexpr uint32_t kSlot16 = TcCfg::kSlotBytes >> 4;
       // S_t(j) = Q_t K_j^T into tile t's S columns.
       auto issue_s = [&](int j, int t) {
-        const uint32_t kb = k0base + (j % TcCfg::kKStages) * TcCfg::kTileBytes;
-        const uint32_t qb = q_base + t * TcCfg::kQBytes;
+        const uint64_t kd = dk + (pos_k(j) % NS) * kSlot16;
+        const uint64_t qd = dq + t * (TcCfg::kQBytes >> 4);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-          umma_bf16_ss(tmem + t * 128, umma_smem_desc_sw128(qb + off, 16, 1024),
-                       umma_smem_desc_sw128(kb + off, 16, 1024), kIdescS, kk > 0 ? 1u : 0u);
+          const uint32_t off = ((kk >> 2) * 16384 + (kk & 3) * 32) >> 4;
+          umma_bf16_ss(tmem + t * 128, qd + off, kd + off, kIdescS, kk > 0 ? 1u : 0u);
         }
         umma_commit(&s_full[t]);
       };
-      if (nblk > 0) {
-        ok = wait_k(0);
-        if (ok) {
-          for (int t = 0; t < 2; ++t)
-            if (nblk_t[t] > 0) issue_s(0, t);
-          umma_commit(&k_empty[0]);
-        }
+      if (nblk > 0 && (ok = wait_slot(pos_k(0)))) {
+        for (int t = 0; t < 2; ++t)
+          if (nblk_t[t] > 0) issue_s(0, t);
+        umma_commit(&slot_empty[pos_k(0) % NS]);
       }
       for (int j = 0; ok && j < nblk; ++j) {
-        if (*abort_flag ||
-            !mbar_wait(&v_full[j % TcCfg::kVStages], (j / TcCfg::kVStages) & 1)) {
-          ok = false;
-          break;
+        if (j + 1 < nblk) {
+          if (!(ok = wait_slot(pos_k(j + 1)))) break;
+          for (int t = 0; t < 2; ++t) {
+            if (j + 1 < nblk_t[t]) {
+              if (!mbar_wait_mma(&s_free[t], j & 1, abort_flag)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              issue_s(j + 1, t);
+            }
+          }
+          if (!ok) break;
+          umma_commit(&slot_empty[pos_k(j + 1) % NS]);
         }
-        const uint32_t vb = v0base + (j % TcCfg::kVStages) * TcCfg::kTileBytes;
-        bool k_next = false;
+        if (!(ok = wait_slot(pos_v(j)))) break;
+        const uint64_t vd = dv + (pos_v(j) % NS) * kSlot16;
         for (int t = 0; t < 2; ++t) {
           if (j < nblk_t[t]) {
-            if (*abort_flag || !mbar_wait(&p_full[t], j & 1)) {
+            if (!mbar_wait_mma(&p_full[t], j & 1, abort_flag)) {
               ok = false;
               break;
             }
             tc_fence_after();
 #pragma unroll
             for (int kk = 0; kk < 8; ++kk)
-              umma_bf16_ts(tmem + TcCfg::kOCol + t * 128, tmem + t * 128 + kk * 8,
-                           umma_smem_desc_sw128(vb + kk * 2048, 16384, 1024), kIdescPV,
-                           (j > 0 || kk > 0) ? 1u : 0u);
-            umma_commit(&o_ready[t]);
-          }
-          if (j + 1 < nblk_t[t]) {
-            if (!k_next && !(ok = k_next = wait_k(j + 1))) break;
-            issue_s(j + 1, t);
+              umma_bf16_ss(tmem + TcCfg::kOCol + t * 128,
+                           dp + t * (TcCfg::kQBytes >> 4) +
+                               (((kk >> 2) * 16384 + (kk & 3) * 32) >> 4),
+                           vd + kk * (kPageBytes >> 4), kIdescPV, (j > 0 || kk > 0) ? 1u : 0u);
+            umma_commit(&pv_done[t]);
           }
         }
         if (!ok) break;
-        umma_commit(&v_empty[j % TcCfg::kVStages]);
-        if (k_next) umma_commit(&k_empty[(j + 1) % TcCfg::kKStages]);
+        umma_commit(&slot_empty[pos_v(j) % NS]);
       }
       if (!ok) {
         atomicOr(&g_status_word, kErrTimeout);
@@ -391,55 +395,120 @@ __global__ void __launch_bounds__(TcCfg::kThreads, 1)
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const uint32_t s_addr = tmem + lane_base + t * 128;
     const uint32_t o_addr = tmem + lane_base + TcCfg::kOCol + t * 128;
+    const uint32_t p_row = smem_u32(smem + TcCfg::kPOff + t * TcCfg::kQBytes) + r * 128;
+    const uint32_t r7 = static_cast<uint32_t>(r & 7);
     const float ninf = -INFINITY;
+    const float2 sc2 = make_float2(a.scale_log2, a.scale_log2);
     float m = ninf, l = 0.f;
     bool ok = true;
     for (int j = 0; j < nb; ++j) {
-      ok = __all_sync(0xffffffffu, *abort_flag == 0 && mbar_wait(&s_full[t], j & 1));
+      ok = __all_sync(0xffffffffu, mbar_wait_fast(&s_full[t], j & 1, abort_flag));
       if (!ok) break;
-      // O += P_{j-1} V_{j-1} was issued before S_t(j), and MMAs complete in order, so o_ready
-      // (j-1) is already complete here.  It is still waited on every block, in order, so a parity
-      // wait is never satisfied by an older phase.
-      if (j > 0) {
-        ok = __all_sync(0xffffffffu, *abort_flag == 0 && mbar_wait(&o_ready[t], (j - 1) & 1));
-        if (!ok) break;
-      }
       tc_fence_after();
       const int k0 = key_lo + j * TcCfg::kBlockKeys;
       const bool need_mask =
           (k0 + TcCfg::kBlockKeys - 1 > qpos) || (k0 + TcCfg::kBlockKeys > key_end);
       const bool warp_masks = __any_sync(0xffffffffu, need_mask);
-
-      // Row max, then p against the running max m, which only moves (and O is rescaled) when the
-      // block's max exceeds it by more than 2^8.
-      const float mx = softmax_max_pass(s_addr, need_mask, k0, qpos, key_end) * a.scale_log2;
+      // Row max over all 128 scores; then the exponentials of the first 64 from registers, and of
+      // the last 64 from a second read of TMEM (holding all 128 scores and 64 packed P words at
+      // once does not fit the register budget).  S_t is released after that second read.
+      float mx;
+      float2 suma[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) suma[i] = make_float2(0.f, 0.f);
+      uint32_t pk[4][16];
       float alpha = 1.f;
       bool rescale = false;
-      if (mx > m + 8.f) {
-        alpha = fast_exp2(m - mx);
-        rescale = j > 0;
-        m = mx;
+      {
+        float s0[32], s1[32];
+        {
+          float s2[32], s3[32];
+          tmem_ld32(s_addr, s0);
+          tmem_ld32(s_addr + 32, s1);
+          tmem_ld32(s_addr + 64, s2);
+          tmem_ld32(s_addr + 96, s3);
+          tmem_wait_ld();
+          if (need_mask) {
+            mask_scores32(s0, k0, qpos, key_end);
+            mask_scores32(s1, k0 + 32, qpos, key_end);
+            mask_scores32(s2, k0 + 64, qpos, key_end);
+            mask_scores32(s3, k0 + 96, qpos, key_end);
+          }
+          mx = max128(s0, s1, s2, s3) * a.scale_log2;
+        }
+        // The running max m only moves (and O is rescaled) when the block's max exceeds it by
+        // more than 2^8.
+        if (mx > m + 8.f) {
+          alpha = fast_exp2(m - mx);
+          rescale = j > 0;
+          m = mx;
+        }
+        const float neg_mu = m == ninf ? 0.f : -m;
+        const float2 nm2 = make_float2(neg_mu, neg_mu);
+        if (warp_masks) {
+          exp_pack32<true>(s0, sc2, nm2, suma, pk[0]);
+          exp_pack32<true>(s1, sc2, nm2, suma, pk[1]);
+        } else {
+          exp_pack32<false>(s0, sc2, nm2, suma, pk[0]);
+          exp_pack32<false>(s1, sc2, nm2, suma, pk[1]);
+        }
+        pin16(pk[0]);
+        pin16(pk[1]);
       }
-      const float neg_mu = m == ninf ? 0.f : -m;
-      const float sum =
-          warp_masks ? softmax_exp_pass<true>(s_addr, a.scale_log2, neg_mu, k0, qpos, key_end)
-                     : softmax_exp_pass<false>(s_addr, a.scale_log2, neg_mu, k0, qpos, key_end);
-      l = l * alpha + sum;
+      {
+        float s2[32], s3[32];
+        tmem_ld32(s_addr + 64, s2);
+        tmem_ld32(s_addr + 96, s3);
+        tmem_wait_ld();
+        tc_fence_before();
+        mbar_arrive(&s_free[t]);  // the MMA may now overwrite S_t with S_t(j + 1)
+        const float neg_mu = m == ninf ? 0.f : -m;
+        const float2 nm2 = make_float2(neg_mu, neg_mu);
+        if (warp_masks) {
+          if (need_mask) {
+            mask_scores32(s2, k0 + 64, qpos, key_end);
+            mask_scores32(s3, k0 + 96, qpos, key_end);
+          }
+          exp_pack32<true>(s2, sc2, nm2, suma, pk[2]);
+          exp_pack32<true>(s3, sc2, nm2, suma, pk[3]);
+        } else {
+          exp_pack32<false>(s2, sc2, nm2, suma, pk[2]);
+          exp_pack32<false>(s3, sc2, nm2, suma, pk[3]);
+        }
+      }
+      const float2 s01 = __fadd2_rn(suma[0], suma[1]);
+      const float2 s23 = __fadd2_rn(suma[2], suma[3]);
+      const float2 st = __fadd2_rn(s01, s23);
+      l = l * alpha + (st.x + st.y);
 
-      // O holds sum_{i<j} P_i V_i; rescale it when the max moved (rare after the first block).
-      if (j > 0 && __any_sync(0xffffffffu, rescale)) {
+      // This tile's previous P*V must be complete before its P buffer is overwritten and before
+      // O is rescaled.  It is waited on every block, in order, so a parity wait is never
+      // satisfied by an older phase; it was issued a whole block ago, so the wait is normally free.
+      if (j > 0) {
+        ok = __all_sync(0xffffffffu, mbar_wait_fast(&pv_done[t], (j - 1) & 1, abort_flag));
+        if (!ok) break;
+        tc_fence_after();
+      }
+      const bool any_rescale = __any_sync(0xffffffffu, rescale);
+      if (j > 0 && any_rescale) {
         const float f = rescale ? alpha : 1.f;
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          float ov[32];
-          tmem_ld32(o_addr + c * 32, ov);
+        for (int c = 0; c < 16; ++c) {
+          float ov[8];
+          tmem_ld8(o_addr + c * 8, ov);
           tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) ov[i] *= f;
-          tmem_st32(o_addr + c * 32, ov);
+          for (int i = 0; i < 8; ++i) ov[i] *= f;
+          tmem_st8(o_addr + c * 8, ov);
         }
         tmem_wait_st();
       }
+#pragma unroll
+      for (int u = 0; u < 16; ++u) {
+        const int c = u >> 2, i = (u & 3) * 4;
+        st_shared_v4(p_row + (u >> 3) * 16384 + (((u & 7) ^ r7) << 4), pk[c][i], pk[c][i + 1],
+                     pk[c][i + 2], pk[c][i + 3]);
+      }
+      fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(&p_full[t]);
     }
@@ -449,7 +518,8 @@ __global__ void __launch_bounds__(TcCfg::kThreads, 1)
         *abort_flag = 1;
       }
     } else if (nb > 0) {
-      ok = __all_sync(0xffffffffu, mbar_wait(&o_ready[t], (nb - 1) & 1));
+      // This tile's last P*V (the phase before it was waited on in the last block).
+      ok = __all_sync(0xffffffffu, mbar_wait_fast(&pv_done[t], (nb - 1) & 1, abort_flag));
       if (!ok && lane == 0) {
         atomicOr(&g_status_word, kErrTimeout);
         *abort_flag = 1;
