@@ -7,32 +7,35 @@
 // range of the sequence's KV pages, walked in blocks of 128 keys.
 //
 //   warps 0-3   softmax for tile A, warps 4-7 softmax for tile B: one thread per row (TMEM lane).
-//               Per block: load the row's 128 scores from TMEM into registers and release the S
-//               columns at once (the next S of this tile can start), causal / range mask (cached
-//               length as offset), row max, p = 2^(s*scale*log2e - m) (3 of 8 pairs on the FMA
-//               pipe), row sum, and P packed to bf16 in registers; then, once this tile's previous
-//               P*V has finished with its P buffer in shared memory, P is stored there.  The
-//               running max only moves (and O in TMEM is rescaled) when it grows by more than 2^8.
+//               Per block: read the row's 128 scores from TMEM, causal / range mask (cached length
+//               as offset), row max, p = 2^(s*scale*log2e - m) (3 of 8 pairs on the FMA pipe) for
+//               the first 64, a second read of the last 64 (registers do not hold 128 scores and 64
+//               packed P words at once), release of the S columns (the next S can start), the
+//               rest of p, row sum, and P packed to bf16 in registers; then, once this tile's
+//               previous P*V has finished with its P buffer in shared memory, P is stored there.
+//               The running max only moves (and O in TMEM is rescaled) when it grows by more
+//               than 2^8.
 //   warp 8      TMA producer: K and V blocks in consumption order K_0, K_1, V_0, K_2, V_1, ... into
 //               a 3-slot ring of 32 KiB.  K: 16 boxes of 2 KiB (8 pages x two 64-dim halves), laid
 //               out as [half][128 keys][64] for the K-major operand; V: 8 boxes of 4 KiB (one page
 //               each), read as an MN-major operand one page per 16-key step.  One box per lane;
 //               pages past the item's range are read from an out-of-range block id, which the TMA
 //               unit fills with zeros.
-//   warp 9      TMEM allocator (512 columns) and, on one thread, the MMA issuer; every MMA takes
-//               both operands from shared memory (an operand in TMEM runs at half rate):
-//                 S_t(j+1) = Q_t K_{j+1}^T  (M=128, N=128, K=128) as soon as S_t(j) is in registers
-//                 O_t     += P_t(j) V_j     (M=128, N=128, K=128) as soon as P_t(j) is stored
-//               in the order S_A(j+1) S_B(j+1) O_A(j) O_B(j), so the scores of the next block are
-//               ready before the softmax needs them and the tensor core never waits for a P store
-//               of the same block.  P in shared memory, not TMEM: tcgen05.st traffic slows the
-//               tensor core, plain shared-memory stores do not.
+//   warps 9, 10 MMA issuers (warp 9 also allocates the 512 TMEM columns); every MMA takes both
+//               operands from shared memory, P included:
+//                 warp 9:  S_t(j) = Q_t K_j^T  (M=128, N=128, K=128) once both tiles hold S(j-1)
+//                          in registers
+//                 warp 10: O_t += P_t(j) V_j   (M=128, N=128, K=128) once both P(j) are stored
+//               One thread's MMA issue queue is shallow, so a wait in a single issuer idles the
+//               tensor core; with two independent streams one keeps it busy while the other waits.
+//               The scores of the next block are ready before the softmax needs them and the
+//               tensor core never waits for a P store of the same block.  P goes through shared
+//               memory, not TMEM: tcgen05.st traffic slows the tensor core, plain stores do not.
 //
 // TMEM columns: S_A at 0, S_B at 128, O_A at 256, O_B at 384.  Shared memory: Q_A, Q_B, P_A, P_B
 // (each [2 halves][128 rows][64] bf16, K-major) and the K/V ring, all 128-byte swizzled with
-// 8-row atoms 1024 bytes apart.  Every wait is
-// bounded; on a timeout the CTA records kErrTimeout, stops, lets issued MMAs and TMA copies
-// finish, frees TMEM and exits.
+// 8-row atoms 1024 bytes apart.  Every wait is bounded; on a timeout the CTA records
+// kErrTimeout, stops, lets issued MMAs and TMA copies finish, frees TMEM and exits.
 #pragma once
 
 #include "paged_attention.cuh"
@@ -41,7 +44,7 @@
 namespace ms {
 
 struct TcCfg {
-  static constexpr int kThreads = 320;
+  static constexpr int kThreads = 352;
   static constexpr int kSlots = 3;          // K/V ring slots (one 128-key K or V block each)
   static constexpr int kTileTokens = 64;    // query tokens per 128-row tile
   static constexpr int kItemTokens = 128;   // query tokens per work item (two tiles)
@@ -52,7 +55,7 @@ struct TcCfg {
   static constexpr int kPOff = 2 * kQBytes;                // P_A, P_B
   static constexpr int kRingOff = kPOff + 2 * kQBytes;     // K/V ring
   static constexpr int kBarOff = kRingOff + kSlots * kSlotBytes;
-  static constexpr int kNumBars = 2 * kSlots + 2 + 2 + 2 + 2 + 1;
+  static constexpr int kNumBars = 2 * kSlots + 2 + 1 + 1 + 2 + 1;
   static constexpr int kSmemBytes = 1024 + kBarOff + (kNumBars + 2) * 8;
   static_assert(kSmemBytes <= 232448, "shared memory budget");
   static constexpr uint32_t kTmemCols = 512;
@@ -168,9 +171,9 @@ __global__ void __launch_bounds__(TcCfg::kThreads, 1)
   uint64_t* slot_full = bars;              // [NS]
   uint64_t* slot_empty = slot_full + NS;   // [NS]
   uint64_t* s_full = slot_empty + NS;      // [tile]: S_t(j) computed
-  uint64_t* s_free = s_full + 2;           // [tile]: S_t(j) read into registers
-  uint64_t* p_full = s_free + 2;           // [tile]: P_t(j) stored (and O_t rescaled)
-  uint64_t* pv_done = p_full + 2;          // [tile]: O_t += P_t(j) V_j finished
+  uint64_t* s_free = s_full + 2;           // both tiles' S(j) read into registers
+  uint64_t* p_full = s_free + 1;           // both tiles' P(j) stored (and O rescaled)
+  uint64_t* pv_done = p_full + 1;          // [tile]: O_t += P_t(j) V_j finished
   uint64_t* mma_drain = pv_done + 2;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + TcCfg::kNumBars);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + TcCfg::kNumBars + 1);
@@ -210,11 +213,12 @@ __global__ void __launch_bounds__(TcCfg::kThreads, 1)
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(&s_full[t], 1);
-      mbar_init(&s_free[t], 128);
-      mbar_init(&p_full[t], 128);
       mbar_init(&pv_done[t], 1);
     }
-    mbar_init(mma_drain, 1);
+    // One phase per block for both tiles (see the softmax's arrive count).
+    mbar_init(s_free, 256);
+    mbar_init(p_full, 256);
+    mbar_init(mma_drain, 2);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -302,85 +306,76 @@ __global__ void __launch_bounds__(TcCfg::kThreads, 1)
         }
       }
     }
-  } else if (warp == 9) {
-    // ---------------- MMA issuer ----------------
+  } else if (warp == 9 || warp == 10) {
+    // ---------------- MMA issuers: warp 9 issues every S = Q K^T, warp 10 every O += P V ------
+    // Two issuing threads, two independent MMA streams (different TMEM columns and operands): the
+    // issue queue of one thread is shallow, so any wait in a single issuer would leave the tensor
+    // core idle; with two, one stream keeps it busy while the other waits.  tcgen05.commit tracks
+    // the MMAs of the committing thread only, so each stream signals its own barriers.
     if (lane == 0) {
+      const bool is_pv = warp == 10;
       constexpr uint32_t kIdescS = umma_idesc_bf16(128, 128, false);
       constexpr uint32_t kIdescPV = umma_idesc_bf16(128, 128, true);
-      const uint32_t q_base = smem_u32(smem + TcCfg::kQOff);
-      const uint32_t p_base = smem_u32(smem + TcCfg::kPOff);
       const uint32_t ring = smem_u32(smem + TcCfg::kRingOff);
       bool ok = true;
       auto wait_slot = [&](int p) -> bool {
-        if (!mbar_wait_mma(&slot_full[p % NS], (p / NS) & 1, abort_flag)) return false;
-        tc_fence_after();
-        return true;
+        return mbar_wait_mma(&slot_full[p % NS], (p / NS) & 1, abort_flag);
       };
       // Descriptors are built once; operand offsets are added to their start-address field
       // (shared-memory addresses >> 4 fit its 14 bits with room to spare).
-      const uint64_t dq = umma_smem_desc_sw128(q_base, 16, 1024);
-      const uint64_t dp = umma_smem_desc_sw128(p_base, 16, 1024);
+      const uint64_t dq = umma_smem_desc_sw128(smem_u32(smem + TcCfg::kQOff), 16, 1024);
+      const uint64_t dp = umma_smem_desc_sw128(smem_u32(smem + TcCfg::kPOff), 16, 1024);
       const uint64_t dk = umma_smem_desc_sw128(ring, 16, 1024);
       const uint64_t dv = umma_smem_desc_sw128(ring, 2048, 1024);  // [page][half][16 keys][64]
       constexpr uint32_t kSlot16 = TcCfg::kSlotBytes >> 4;
-      // S_t(j) = Q_t K_j^T into tile t's S columns.
-      auto issue_s = [&](int j, int t) {
-        const uint64_t kd = dk + (pos_k(j) % NS) * kSlot16;
-        const uint64_t qd = dq + t * (TcCfg::kQBytes >> 4);
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t off = ((kk >> 2) * 16384 + (kk & 3) * 32) >> 4;
-          umma_bf16_ss(tmem + t * 128, qd + off, kd + off, kIdescS, kk > 0 ? 1u : 0u);
-        }
-        umma_commit(&s_full[t]);
-      };
-      if (nblk > 0 && (ok = wait_slot(pos_k(0)))) {
-        for (int t = 0; t < 2; ++t)
-          if (nblk_t[t] > 0) issue_s(0, t);
-        umma_commit(&slot_empty[pos_k(0) % NS]);
-      }
-      for (int j = 0; ok && j < nblk; ++j) {
-        if (j + 1 < nblk) {
-          if (!(ok = wait_slot(pos_k(j + 1)))) break;
+      if (!is_pv) {
+        // S_t(j) = Q_t K_j^T into tile t's S columns, as soon as both tiles hold S(j-1) in
+        // registers and K_j has landed.
+        for (int j = 0; ok && j < nblk; ++j) {
+          if (!(ok = wait_slot(pos_k(j)) && (j == 0 || mbar_wait_mma(s_free, (j - 1) & 1,
+                                                                      abort_flag))))
+            break;
+          tc_fence_after();
+          const uint64_t kd = dk + (pos_k(j) % NS) * kSlot16;
           for (int t = 0; t < 2; ++t) {
-            if (j + 1 < nblk_t[t]) {
-              if (!mbar_wait_mma(&s_free[t], j & 1, abort_flag)) {
-                ok = false;
-                break;
-              }
-              tc_fence_after();
-              issue_s(j + 1, t);
-            }
-          }
-          if (!ok) break;
-          umma_commit(&slot_empty[pos_k(j + 1) % NS]);
-        }
-        if (!(ok = wait_slot(pos_v(j)))) break;
-        const uint64_t vd = dv + (pos_v(j) % NS) * kSlot16;
-        for (int t = 0; t < 2; ++t) {
-          if (j < nblk_t[t]) {
-            if (!mbar_wait_mma(&p_full[t], j & 1, abort_flag)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
+            if (j < nblk_t[t]) {
+              const uint64_t qd = dq + t * (TcCfg::kQBytes >> 4);
 #pragma unroll
-            for (int kk = 0; kk < 8; ++kk)
-              umma_bf16_ss(tmem + TcCfg::kOCol + t * 128,
-                           dp + t * (TcCfg::kQBytes >> 4) +
-                               (((kk >> 2) * 16384 + (kk & 3) * 32) >> 4),
-                           vd + kk * (kPageBytes >> 4), kIdescPV, (j > 0 || kk > 0) ? 1u : 0u);
-            umma_commit(&pv_done[t]);
+              for (int kk = 0; kk < 8; ++kk) {
+                const uint32_t off = ((kk >> 2) * 16384 + (kk & 3) * 32) >> 4;
+                umma_bf16_ss(tmem + t * 128, qd + off, kd + off, kIdescS, kk > 0 ? 1u : 0u);
+              }
+              umma_commit(&s_full[t]);
+            }
           }
+          umma_commit(&slot_empty[pos_k(j) % NS]);
         }
-        if (!ok) break;
-        umma_commit(&slot_empty[pos_v(j) % NS]);
+      } else {
+        // O_t += P_t(j) V_j once both tiles' P(j) are stored and V_j has landed.
+        for (int j = 0; ok && j < nblk; ++j) {
+          if (!(ok = wait_slot(pos_v(j)) && mbar_wait_mma(p_full, j & 1, abort_flag))) break;
+          tc_fence_after();
+          const uint64_t vd = dv + (pos_v(j) % NS) * kSlot16;
+          for (int t = 0; t < 2; ++t) {
+            if (j < nblk_t[t]) {
+#pragma unroll
+              for (int kk = 0; kk < 8; ++kk)
+                umma_bf16_ss(tmem + TcCfg::kOCol + t * 128,
+                             dp + t * (TcCfg::kQBytes >> 4) +
+                                 (((kk >> 2) * 16384 + (kk & 3) * 32) >> 4),
+                             vd + kk * (kPageBytes >> 4), kIdescPV, (j > 0 || kk > 0) ? 1u : 0u);
+              umma_commit(&pv_done[t]);
+            }
+          }
+          umma_commit(&slot_empty[pos_v(j) % NS]);
+        }
       }
       if (!ok) {
         atomicOr(&g_status_word, kErrTimeout);
         *abort_flag = 1;
       }
-      // Every MMA issued so far must finish before TMEM is freed or the CTA exits.
+      // Every MMA issued so far (by both issuers) must finish before TMEM is freed or the CTA
+      // exits: each issuer commits once to mma_drain (two arrivals complete it).
       umma_commit(mma_drain);
       if (!mbar_wait(mma_drain, 0)) atomicOr(&g_status_word, kErrTimeout);
     }
@@ -405,6 +400,9 @@ __global__ void __launch_bounds__(TcCfg::kThreads, 1)
       ok = __all_sync(0xffffffffu, mbar_wait_fast(&s_full[t], j & 1, abort_flag));
       if (!ok) break;
       tc_fence_after();
+      // s_free and p_full complete once per block with 256 arrivals: a tile whose partner has no
+      // block j (tile A's blocks end first; tile B may have none) arrives for both.
+      const uint32_t arrive_cnt = j < nblk_t[1 - t] ? 1u : 2u;
       const int k0 = key_lo + j * TcCfg::kBlockKeys;
       const bool need_mask =
           (k0 + TcCfg::kBlockKeys - 1 > qpos) || (k0 + TcCfg::kBlockKeys > key_end);
@@ -461,7 +459,7 @@ __global__ void __launch_bounds__(TcCfg::kThreads, 1)
         tmem_ld32(s_addr + 96, s3);
         tmem_wait_ld();
         tc_fence_before();
-        mbar_arrive(&s_free[t]);  // the MMA may now overwrite S_t with S_t(j + 1)
+        mbar_arrive_cnt(s_free, arrive_cnt);  // the MMA may now overwrite S_t with S_t(j + 1)
         const float neg_mu = m == ninf ? 0.f : -m;
         const float2 nm2 = make_float2(neg_mu, neg_mu);
         if (warp_masks) {
@@ -510,7 +508,7 @@ __global__ void __launch_bounds__(TcCfg::kThreads, 1)
       }
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(&p_full[t]);
+      mbar_arrive_cnt(p_full, arrive_cnt);
     }
     if (!ok) {
       if (lane == 0) {
