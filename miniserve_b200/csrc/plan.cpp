@@ -7,8 +7,11 @@
 // its own block table (CSR), and the work is cut into (query tile, KV page range) items:
 //   * a sequence with <= 8 new tokens (decode, speculative verify) is one decode tile;
 //   * a chunk of 9..64 tokens is one tile for the mma.sync tile kernel;
-//   * a chunk of more than 64 tokens is cut into items of 128 query tokens (two 128-row tiles)
-//     for the tcgen05 tensor-core kernel, whose page ranges are split in whole 128-key blocks;
+//   * a chunk of more than 64 tokens is cut into items of two 64-token query tiles (2 x 128 rows)
+//     for the tcgen05 tensor-core kernel: groups g and G-1-g of the chunk when no item of the
+//     chunk is split (equal causal work per item), else adjacent groups, whose page ranges are
+//     split in whole 128-key blocks.  Tensor-core records carry tile A as (tok0, n_q) and tile B
+//     as fields 6 and 7 (first token, count; count 0 for no tile B);
 //   * a tile's visible pages, ceil((num_cached + tok0 + n_q) / 16), are split into near-equal
 //     ranges of at most `pages_per_split` pages; split tiles get partial rows in the workspace
 //     and a combine record.
@@ -34,14 +37,20 @@ constexpr int kTcTokens = 128;       // query tokens per tensor-core work item (
 constexpr int kItemsPerSm = 1;       // automatic split: about one item per SM per KV head
 constexpr int kMinSplitPages = 32;   // a split streams at least 256 KiB per KV head
 constexpr int kTcBlockPages = 8;     // 128-key blocks of the tensor-core kernel
-constexpr int kTcMinSplitPages = 32; // tensor-core items cover at least 4 blocks
-// Splitting a tensor-core item's keys costs a combine over 256 partial rows, which only pays when
-// the items alone cannot occupy the GPU: with at least this many items per 16 SMs (x 8 KV heads,
-// i.e. half the SMs busy), they are not split.
-constexpr int kTcNoSplitItemsPer16Sms = 1;
+constexpr int kTcMinSplitPages = 32; // forced splits: tensor-core items cover at least 4 blocks
+// Automatic tensor-core plan.  The planner does not see the head count; it sizes work for
+// kTcAssumedKvHeads CTAs per item (Qwen3-0.6B's 8 KV heads), which only affects speed.
+//  * When the unsplit items already fill one wave (items x heads >= SMs), they stay whole and
+//    adjacent; longest-first order packs the waves.
+//  * Otherwise key ranges are split so that about one wave of CTAs results, but never below
+//    kTcAutoMinSplitPages (each CTA's start-up is worth about two blocks of work), and a chunk
+//    that needs no split pairs its 64-token groups zig-zag so the items of the wave cost alike.
+constexpr int kTcAssumedKvHeads = 8;
+constexpr int kTcAutoMinSplitPages = 128;
 
 struct Item {
   int seq, tok0, n_q, pb, pe, part_row;
+  int tok_b = 0, n_b = 0;  // tensor-core items: tile B's first token and token count
 };
 
 int64_t round4(int64_t x) { return (x + 3) & ~int64_t(3); }
@@ -133,20 +142,62 @@ extern "C" int ms_plan_build(int32_t num_seqs, const int32_t* flat_start, const 
 
   std::vector<Item> dec, til, tcv, comb;
   int64_t part_rows = 0;
-  int64_t n_tc_tiles = 0;
-  for (const Item& t : tiles) n_tc_tiles += num_new[t.seq] > kTileTokens ? 1 : 0;
-  int tc_split = std::max(kTcMinSplitPages, (split + kTcBlockPages - 1) / kTcBlockPages * kTcBlockPages);
-  if (pages_per_split == 0 && n_tc_tiles * 16 >= static_cast<int64_t>(num_sms) * kTcNoSplitItemsPer16Sms)
-    tc_split = 1 << 30;
+  int64_t n_tc_tiles = 0, tc_pages = 0;
+  for (const Item& t : tiles) {
+    if (num_new[t.seq] > kTileTokens) {
+      ++n_tc_tiles;
+      tc_pages += t.pe;
+    }
+  }
+  auto round_blocks = [](int64_t p) { return (p + kTcBlockPages - 1) / kTcBlockPages * kTcBlockPages; };
+  int64_t tc_split64;
+  if (pages_per_split > 0) {
+    tc_split64 = std::max<int64_t>(kTcMinSplitPages, round_blocks(pages_per_split));
+  } else if (n_tc_tiles * kTcAssumedKvHeads >= num_sms) {
+    tc_split64 = int64_t(1) << 30;
+  } else {
+    const int64_t per_cta = (tc_pages * kTcAssumedKvHeads + num_sms - 1) / std::max(num_sms, 1);
+    tc_split64 = std::max<int64_t>(kTcAutoMinSplitPages, round_blocks(per_cta));
+  }
+  const int tc_split = static_cast<int>(std::min<int64_t>(tc_split64, int64_t(1) << 30));
+  const bool tc_zigzag = pages_per_split > 0 || n_tc_tiles * kTcAssumedKvHeads < num_sms;
   for (const Item& t : tiles) {
     const int pages = t.pe;
     const int nn = num_new[t.seq];
     const bool is_tc = nn > kTileTokens;
+    if (is_tc) {
+      // A chunk none of whose items is split pairs its 64-token groups zig-zag: tile A = group
+      // g, tile B = group G-1-g.  Causal work grows with the group index, so every pair costs
+      // about the same and the slowest item no longer sets the kernel's time.
+      const int64_t c = num_cached[t.seq];
+      const int64_t chunk_pages = (c + nn + block_size - 1) / block_size;
+      if (tc_zigzag && chunk_pages <= tc_split) {
+        if (t.tok0 != 0) continue;  // the whole chunk is emitted with its first tile
+        const int groups = (nn + kTileTokens - 1) / kTileTokens;
+        for (int g = 0; g < (groups + 1) / 2; ++g) {
+          const int h = groups - 1 - g;
+          Item it{t.seq, g * kTileTokens, std::min(kTileTokens, nn - g * kTileTokens), 0, 0, -1};
+          if (h > g) {
+            it.tok_b = h * kTileTokens;
+            it.n_b = std::min(kTileTokens, nn - it.tok_b);
+          }
+          const int64_t last = h > g ? it.tok_b + it.n_b : it.tok0 + it.n_q;
+          it.pe = static_cast<int>((c + last + block_size - 1) / block_size);
+          tcv.push_back(it);
+        }
+        continue;
+      }
+    }
     const int sp = is_tc ? tc_split : split;
     const int ns = (pages + sp - 1) / sp;
     std::vector<Item>& dst = nn <= kDecodeMaxTokens ? dec : (is_tc ? tcv : til);
+    // Tensor-core items that are split keep their two tiles adjacent (A = tokens tok0..+63, B =
+    // the next 64), so the partial rows of the item are its tokens in order for the combine.
+    const int n_a = is_tc ? std::min(kTileTokens, t.n_q) : t.n_q;
+    const int tok_b = is_tc ? t.tok0 + kTileTokens : 0;
+    const int n_b = is_tc ? std::max(0, t.n_q - kTileTokens) : 0;
     if (ns <= 1) {
-      dst.push_back({t.seq, t.tok0, t.n_q, 0, pages, -1});
+      dst.push_back({t.seq, t.tok0, n_a, 0, pages, -1, tok_b, n_b});
       continue;
     }
     const int rows = 2 * t.n_q;
@@ -161,8 +212,8 @@ extern "C" int ms_plan_build(int32_t num_seqs, const int32_t* flat_start, const 
     int pb = 0;
     for (int s = 0; s < ns; ++s) {
       const int len = std::min(pages - pb, (base + (s < rem ? 1 : 0)) * unit);
-      dst.push_back({t.seq, t.tok0, t.n_q, pb, pb + len,
-                     static_cast<int>(part_rows + static_cast<int64_t>(s) * rows)});
+      dst.push_back({t.seq, t.tok0, n_a, pb, pb + len,
+                     static_cast<int>(part_rows + static_cast<int64_t>(s) * rows), tok_b, n_b});
       pb += len;
     }
     comb.push_back({t.seq, t.tok0, t.n_q, static_cast<int>(part_rows), ns, 0});
@@ -209,6 +260,8 @@ extern "C" int ms_plan_build(int32_t num_seqs, const int32_t* flat_start, const 
       r[3] = v[k].pb;
       r[4] = v[k].pe;
       r[5] = v[k].part_row;
+      r[6] = v[k].tok_b;
+      r[7] = v[k].n_b;
     }
   };
   put(off_decode, dec);

@@ -183,20 +183,21 @@ __global__ void __launch_bounds__(TcCfg::kThreads, 1)
   const int item_idx = blockIdx.x / a.num_kv;
   const int kvh = blockIdx.x - item_idx * a.num_kv;
   const int* it = a.items + static_cast<long long>(item_idx) * kRec;
-  const int seq = it[0], tok0 = it[1], n_q = it[2], page_begin = it[3], page_end = it[4],
-            part_row = it[5];
+  const int seq = it[0], page_begin = it[3], page_end = it[4], part_row = it[5];
+  // First token (inside the chunk) and token count of tile A and tile B (B's count may be 0).
+  const int tok_a = it[1], n_a = it[2], tok_b = it[6], n_b = it[7];
   const int* sr = a.seqs + static_cast<long long>(seq) * kRec;
   const int flat_start = sr[0], num_cached = sr[2], table_off = sr[4];
   const int npages = page_end - page_begin;
   const int key_lo = page_begin * kBlockTokens;
   const int key_end = page_end * kBlockTokens;
   // Blocks each tile sees inside this item's page range (a tile's last visible key is
-  // num_cached + tok0 + its last token).  Tile A never sees more blocks than tile B.
+  // num_cached + its last token).  Tile A never sees more blocks than tile B, unless B is empty.
   int nblk_t[2];
 #pragma unroll
   for (int t = 0; t < 2; ++t) {
-    const int ntok = min(TcCfg::kTileTokens, n_q - t * TcCfg::kTileTokens);
-    const int vis_end = min(key_end, num_cached + tok0 + t * TcCfg::kTileTokens + ntok);
+    const int ntok = t == 0 ? n_a : n_b;
+    const int vis_end = min(key_end, num_cached + (t == 0 ? tok_a : tok_b) + ntok);
     nblk_t[t] = (ntok <= 0 || vis_end <= key_lo)
                     ? 0
                     : (vis_end - key_lo + TcCfg::kBlockKeys - 1) / TcCfg::kBlockKeys;
@@ -229,14 +230,15 @@ __global__ void __launch_bounds__(TcCfg::kThreads, 1)
   if (warp < 8) {
     // Q tiles: thread r loads row r % 128 of tile r / 128 into the swizzled K-major layout.
     const int t = threadIdx.x >> 7, r = threadIdx.x & 127;
-    const int tok = t * TcCfg::kTileTokens + (r >> 1);
-    const __nv_bfloat16* src = a.q + static_cast<long long>(flat_start + tok0 + tok) * a.q_row_stride +
+    const bool valid = (r >> 1) < (t == 0 ? n_a : n_b);
+    const int tok = (t == 0 ? tok_a : tok_b) + (r >> 1);
+    const __nv_bfloat16* src = a.q + static_cast<long long>(flat_start + tok) * a.q_row_stride +
                                (kvh * kGroup + (r & 1)) * kHeadDim;
     uint8_t* qs = smem + TcCfg::kQOff + t * TcCfg::kQBytes;
 #pragma unroll
     for (int u = 0; u < 16; ++u) {
       uint4 v = make_uint4(0u, 0u, 0u, 0u);
-      if (tok < n_q) v = reinterpret_cast<const uint4*>(src)[u];
+      if (valid) v = reinterpret_cast<const uint4*>(src)[u];
       *reinterpret_cast<uint4*>(qs + tile128_off(r, u)) = v;
     }
     fence_proxy_async_smem();
@@ -384,8 +386,9 @@ __global__ void __launch_bounds__(TcCfg::kThreads, 1)
     // ---------------- softmax warpgroups: thread = row of tile t ----------------
     const int t = warp >> 2;
     const int r = threadIdx.x & 127;
-    const int tok = t * TcCfg::kTileTokens + (r >> 1);
-    const int qpos = num_cached + tok0 + tok;
+    const bool valid = (r >> 1) < (t == 0 ? n_a : n_b);
+    const int tok = (t == 0 ? tok_a : tok_b) + (r >> 1);
+    const int qpos = num_cached + tok;
     const int nb = nblk_t[t];
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const uint32_t s_addr = tmem + lane_base + t * 128;
@@ -527,7 +530,8 @@ __global__ void __launch_bounds__(TcCfg::kThreads, 1)
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
       const int head = kvh * kGroup + (r & 1);
-      const int prow_r = t * 128 + r;  // row inside the item's 2 * n_q partial rows
+      // Row inside the item's partial rows (split items have adjacent tiles: token order).
+      const int prow_r = t * 128 + r;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         float ov[32];
@@ -538,10 +542,10 @@ __global__ void __launch_bounds__(TcCfg::kThreads, 1)
 #pragma unroll
           for (int i = 0; i < 32; ++i) ov[i] = 0.f;
         }
-        if (tok < n_q) {
+        if (valid) {
           if (part_row < 0) {
             __nv_bfloat16* dst = a.out +
-                                 static_cast<long long>(flat_start + tok0 + tok) * a.out_row_stride +
+                                 static_cast<long long>(flat_start + tok) * a.out_row_stride +
                                  head * kHeadDim + c * 32;
 #pragma unroll
             for (int u = 0; u < 4; ++u)

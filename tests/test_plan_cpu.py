@@ -30,42 +30,65 @@ def check_plan(chunks: list[SeqChunk], num_tokens: int, split: int = 0) -> None:
         r = seqs[i]
         assert list(r[:4]) == [c.flat_start, c.num_new, c.num_cached, c.context_len]
         assert list(flat_tables[r[4] : r[4] + r[5]]) == list(c.block_table)
-    # Every query tile's visible pages are covered exactly once by its items.
+    # Every query tile's visible pages are covered exactly once by its items.  Tensor-core
+    # records hold two 64-token tiles: A = (tok0, n_q), B = (fields 6, 7); unsplit chunks pair
+    # groups g and G-1-g, split items keep A and B adjacent.
     cover: dict[tuple[int, int], list[tuple[int, int, int]]] = {}
+    item_tokens: dict[tuple[int, int], int] = {}
+    tc_groups: dict[tuple[int, int], int] = {}
     for kind, items in (("dec", dec), ("til", til), ("tc", tcv)):
         for it in items:
-            seq, tok0, nq, pb, pe, part = (int(x) for x in it[:6])
+            seq, tok0, nq, pb, pe, part, tok_b, n_b = (int(x) for x in it[:8])
             c = chunks[seq]
             assert 0 < nq and tok0 + nq <= c.num_new
             assert 0 <= pb < pe
             if kind == "dec":
-                assert c.num_new <= 8 and tok0 == 0 and nq == c.num_new
+                assert c.num_new <= 8 and tok0 == 0 and nq == c.num_new and tok_b == n_b == 0
+                last = nq
             elif kind == "til":
-                assert 8 < c.num_new <= 64 and tok0 == 0 and nq == c.num_new
+                assert 8 < c.num_new <= 64 and tok0 == 0 and nq == c.num_new and tok_b == n_b == 0
+                last = nq
             else:
-                assert c.num_new > 64 and tok0 % 128 == 0 and nq == min(128, c.num_new - tok0)
+                assert c.num_new > 64 and tok0 % 64 == 0 and nq == min(64, c.num_new - tok0)
                 assert pb % 8 == 0, "tensor-core ranges start on 128-key blocks"
+                for g0, gn in ((tok0, nq), (tok_b, n_b)):
+                    if gn:
+                        assert g0 % 64 == 0 and gn == min(64, c.num_new - g0)
+                        key = (seq, g0)
+                        tc_groups[key] = tc_groups.get(key, 0) + (1 if pb == 0 else 0)
+                if n_b:
+                    assert tok_b > tok0
+                if part >= 0:
+                    assert n_b == 0 or tok_b == tok0 + 64, "split items keep their tiles adjacent"
+                last = tok_b + n_b if n_b else tok0 + nq
+            assert pe <= -(-(c.num_cached + last) // 16)
             cover.setdefault((seq, tok0), []).append((pb, pe, part))
+            item_tokens[(seq, tok0)] = (nq + n_b, -(-(c.num_cached + last) // 16))
         lens = [int(it[4] - it[3]) for it in items]
         assert lens == sorted(lens, reverse=True), "items must be longest first"
-    combos = {(int(r[0]), int(r[1])): r for r in comb}
     for c_idx, c in enumerate(chunks):
-        step = 8 if c.num_new <= 8 else (64 if c.num_new <= 64 else 128)
-        for tok0 in range(0, c.num_new, step):
-            nq = min(step, c.num_new - tok0)
-            pages = -(-(c.num_cached + tok0 + nq) // 16)
-            spans = sorted(cover.pop((c_idx, tok0)))
-            assert spans[0][0] == 0 and spans[-1][1] == pages
-            for a, b in zip(spans, spans[1:]):
-                assert a[1] == b[0]
-            if len(spans) == 1:
-                assert spans[0][2] == -1 and (c_idx, tok0) not in combos
-            else:
-                r = combos[(c_idx, tok0)]
-                assert int(r[2]) == nq and int(r[4]) == len(spans)
-                parts = sorted(s[2] for s in spans)
-                assert parts == [int(r[3]) + k * 2 * nq for k in range(len(spans))]
-    assert not cover
+        if c.num_new > 64:
+            for g0 in range(0, c.num_new, 64):
+                assert tc_groups.pop((c_idx, g0)) == 1, "each 64-token group in exactly one item"
+    assert not tc_groups
+    combos = {(int(r[0]), int(r[1])): r for r in comb}
+    for key, spans in cover.items():
+        spans = sorted(spans)
+        n_tokens, pages = item_tokens[key]
+        assert spans[0][0] == 0 and spans[-1][1] == pages
+        for a, b in zip(spans, spans[1:]):
+            assert a[1] == b[0]
+        if len(spans) == 1:
+            assert spans[0][2] == -1 and key not in combos
+        else:
+            r = combos.pop(key)
+            assert int(r[2]) == n_tokens and int(r[4]) == len(spans)
+            parts = sorted(s[2] for s in spans)
+            assert parts == [int(r[3]) + k * 2 * n_tokens for k in range(len(spans))]
+    assert not combos
+    for c_idx, c in enumerate(chunks):
+        if c.num_new <= 64:
+            assert (c_idx, 0) in cover
     assert info.workspace_bytes_per_kv_head == info.part_rows * 129 * 4
 
 
