@@ -67,7 +67,7 @@ typedef struct MsPlanInfo {
   int32_t num_tokens;
   int32_t n_decode_items;  /* work items of <= 8 query tokens (decode / speculative verify) */
   int32_t n_tile_items;    /* work items of 9..64-token chunks (mma.sync tile kernel) */
-  int32_t n_combine;       /* split tiles whose partials must be merged */
+  int32_t n_combine;       /* split tiles (and cascade rows) whose partials must be merged */
   int32_t off_seqs;        /* int32 offsets of each section inside the packed buffer */
   int32_t off_tables;
   int32_t off_decode;
@@ -83,7 +83,12 @@ typedef struct MsPlanInfo {
   int32_t n_tc_items;      /* work items of 64 query tokens of chunks longer than 64 tokens,
                               run on the tcgen05 tensor-core kernel */
   int32_t off_tc;
-  int32_t reserved[6];
+  int32_t n_cascade;       /* shared-prefix groups: runs of >= 16 consecutive decode / verify
+                              rows whose tables share >= 16 cached blocks attend that prefix
+                              once (tensor-core items over the group's tokens) and merge it with
+                              their own pages; sequence records num_seqs .. num_seqs+n_cascade-1
+                              describe the groups */
+  int32_t reserved[5];
 } MsPlanInfo;
 
 /* Upper bound on the packed buffer length (int32 elements) for a batch of this size. */

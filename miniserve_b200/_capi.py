@@ -58,7 +58,8 @@ class MsPlanInfo(C.Structure):
         ("total_pages", C.c_int64),
         ("n_tc_items", C.c_int32),
         ("off_tc", C.c_int32),
-        ("reserved", C.c_int32 * 6),
+        ("n_cascade", C.c_int32),
+        ("reserved", C.c_int32 * 5),
     ]
 
 

@@ -425,17 +425,22 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const CombineA
   const int seq = cr[0], tok0 = cr[1], n_q = cr[2], part_row0 = cr[3], n_splits = cr[4];
   const int flat_start = a.seqs[static_cast<long long>(seq) * kRec];
   const int rows = n_q * kGroup;
+  // Split s's rows start at part_row0 + s * stride: consecutive (stride = rows) for a split tile;
+  // a cascade row's shared-prefix and own-page partials sit apart (stride in field 5).
+  const int stride = cr[5] != 0 ? cr[5] : rows;
   const int dc = (threadIdx.x & 7) * 16;
   for (int r = threadIdx.x >> 3; r < rows; r += kCombineThreads / 8) {
     float mx = -INFINITY;
     for (int s = 0; s < n_splits; ++s)
-      mx = fmaxf(mx, a.ws_lse[static_cast<long long>(part_row0 + s * rows + r) * a.num_kv + kvh]);
+      mx = fmaxf(mx, a.ws_lse[(static_cast<long long>(part_row0) + static_cast<long long>(s) * stride + r) *
+                                   a.num_kv + kvh]);
     float acc[16];
 #pragma unroll
     for (int i = 0; i < 16; ++i) acc[i] = 0.f;
     float L = 0.f;
     for (int s = 0; s < n_splits; ++s) {
-      const long long prow = static_cast<long long>(part_row0 + s * rows + r) * a.num_kv + kvh;
+      const long long prow =
+          (static_cast<long long>(part_row0) + static_cast<long long>(s) * stride + r) * a.num_kv + kvh;
       const float lse = a.ws_lse[prow];
       const float w = lse == -INFINITY ? 0.f : fast_exp2(lse - mx);
       L += w;

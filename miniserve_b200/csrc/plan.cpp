@@ -15,6 +15,11 @@
 //   * a tile's visible pages, ceil((num_cached + tok0 + n_q) / 16), are split into near-equal
 //     ranges of at most `pages_per_split` pages; split tiles get partial rows in the workspace
 //     and a combine record.
+//   * a run of >= 16 consecutive decode / verify rows, contiguous in the batch, whose block tables
+//     begin with the same >= 16 cached blocks is a cascade group: the shared prefix is attended
+//     once by tensor-core items over all the group's query tokens (a virtual sequence record
+//     after the real ones), each row's remaining pages by an unsplit decode item, and a two-way
+//     combine merges them.
 // Items are ordered longest first so the hardware block scheduler fills the tail with short ones.
 #include <algorithm>
 #include <cstdint>
@@ -47,6 +52,11 @@ constexpr int kTcMinSplitPages = 32; // forced splits: tensor-core items cover a
 //    that needs no split pairs its 64-token groups zig-zag so the items of the wave cost alike.
 constexpr int kTcAssumedKvHeads = 8;
 constexpr int kTcAutoMinSplitPages = 128;
+// Cascade (shared-prefix) attention: a run of consecutive decode / verify rows, contiguous in the
+// batch, whose block tables start with the same whole cached blocks attends that prefix once, as
+// one dense tensor-core problem over all the run's query tokens, instead of once per row.
+constexpr int kCascadeMinRows = 16;
+constexpr int kCascadeMinPages = 16;
 
 struct Item {
   int seq, tok0, n_q, pb, pe, part_row;
@@ -64,8 +74,13 @@ extern "C" int64_t ms_plan_capacity(int32_t num_seqs, int32_t num_tokens,
   // 16 table entries plus one per tile, plus as many combine records.
   const int64_t tiles = static_cast<int64_t>(num_seqs) + num_tokens / kTileTokens + 1;
   const int64_t items = tiles + total_table_entries;
+  // Cascade groups add one sequence record each (at most num_seqs / kCascadeMinRows), tensor-core
+  // items over their query tokens (at most one per 64 tokens plus one per group) and one combine
+  // record per row (within the combine bound above).
+  const int64_t groups = static_cast<int64_t>(num_seqs) / kCascadeMinRows + 1;
   return round4(static_cast<int64_t>(num_seqs) * kRec) + round4(total_table_entries) +
-         3 * round4(items * kRec) + round4(tiles * kRec) + 16;
+         3 * round4(items * kRec) + round4(tiles * kRec) + round4(groups * kRec) +
+         round4((num_tokens / kTileTokens + groups) * kRec) + 16;
 }
 
 extern "C" int ms_plan_build(int32_t num_seqs, const int32_t* flat_start, const int32_t* num_new,
@@ -131,6 +146,54 @@ extern "C" int ms_plan_build(int32_t num_seqs, const int32_t* flat_start, const 
     }
   }
 
+  // Cascade groups: runs of decode / verify rows, consecutive in the batch, whose tables begin
+  // with the same kCascadeMinPages or more whole cached blocks.  cascade_pages[i] is the shared
+  // prefix (in pages) of row i's group, 0 outside groups.
+  struct Group {
+    int first, last, pages, tokens;
+  };
+  std::vector<Group> groups;
+  std::vector<int> cascade_pages(num_seqs, 0);
+  {
+    auto eligible = [&](int i) {
+      return num_new[i] <= kDecodeMaxTokens &&
+             num_cached[i] >= static_cast<int64_t>(kCascadeMinPages) * block_size;
+    };
+    int i = 0;
+    while (i < num_seqs) {
+      if (!eligible(i)) {
+        ++i;
+        continue;
+      }
+      const int32_t* ti = tables + table_offsets[i];
+      int64_t shared = std::min<int64_t>(num_cached[i] / block_size,
+                                         table_offsets[i + 1] - table_offsets[i]);
+      int64_t tokens = num_new[i];
+      int j = i + 1;
+      while (j < num_seqs && eligible(j) &&
+             static_cast<int64_t>(flat_start[j]) == static_cast<int64_t>(flat_start[j - 1]) + num_new[j - 1]) {
+        const int32_t* tj = tables + table_offsets[j];
+        const int64_t cap = std::min<int64_t>(shared, num_cached[j] / block_size);
+        int64_t l = 0;
+        while (l < cap && tj[l] == ti[l]) ++l;
+        if (l < kCascadeMinPages) break;
+        shared = l;
+        tokens += num_new[j];
+        ++j;
+      }
+      if (j - i >= kCascadeMinRows && tokens > kTileTokens) {
+        groups.push_back({i, j, static_cast<int>(shared), static_cast<int>(tokens)});
+        for (int k = i; k < j; ++k) {
+          cascade_pages[k] = static_cast<int>(shared);
+          short_pages -= shared;
+        }
+        i = j;
+      } else {
+        ++i;
+      }
+    }
+  }
+
   // Split size for the bandwidth-bound kernels: enough items to fill the GPU several times
   // over, but never so short that a CTA's start-up latency dominates its streaming.
   int split = pages_per_split;
@@ -165,6 +228,7 @@ extern "C" int ms_plan_build(int32_t num_seqs, const int32_t* flat_start, const 
     const int pages = t.pe;
     const int nn = num_new[t.seq];
     const bool is_tc = nn > kTileTokens;
+    if (cascade_pages[t.seq] > 0) continue;  // planned with its cascade group below
     if (is_tc) {
       // A chunk none of whose items is split pairs its 64-token groups zig-zag: tile A = group
       // g, tile B = group G-1-g.  Causal work grows with the group index, so every pair costs
@@ -219,13 +283,45 @@ extern "C" int ms_plan_build(int32_t num_seqs, const int32_t* flat_start, const 
     comb.push_back({t.seq, t.tok0, t.n_q, static_cast<int>(part_rows), ns, 0});
     part_rows += static_cast<int64_t>(ns) * rows;
   }
+  // Cascade groups.  The shared prefix is attended once by tensor-core items over a virtual
+  // sequence (record num_seqs + g): the group's query tokens, contiguous in the batch, with the
+  // prefix as their cached context, so every prefix key is visible to every query.  Its items
+  // write partial rows for all the group's tokens; each row then attends its own pages after the
+  // prefix with an unsplit decode item, and a two-way combine (split stride in field 5) merges.
+  for (size_t g = 0; g < groups.size(); ++g) {
+    const Group& G = groups[g];
+    if (part_rows + 4 * static_cast<int64_t>(G.tokens) >= (int64_t(1) << 31)) {
+      ms_host::set_error("ms_plan_build: too many partial rows");
+      return MS_ERR_PLAN;
+    }
+    const int vseq = num_seqs + static_cast<int>(g);
+    const int64_t prefix_base = part_rows;
+    part_rows += 2 * static_cast<int64_t>(G.tokens);
+    for (int tok = 0; tok < G.tokens; tok += kTcTokens) {
+      const int nq = std::min(kTcTokens, G.tokens - tok);
+      tcv.push_back({vseq, tok, std::min(kTileTokens, nq), 0, G.pages,
+                     static_cast<int>(prefix_base + 2 * tok), tok + kTileTokens,
+                     std::max(0, nq - kTileTokens)});
+    }
+    for (int k = G.first; k < G.last; ++k) {
+      const int n = num_new[k];
+      const int pages = static_cast<int>((static_cast<int64_t>(num_cached[k]) + n + block_size - 1) / block_size);
+      const int64_t unique_row = part_rows;
+      part_rows += 2 * n;
+      dec.push_back({k, 0, n, G.pages, pages, static_cast<int>(unique_row)});
+      const int64_t prefix_row = prefix_base + 2 * (static_cast<int64_t>(flat_start[k]) - flat_start[G.first]);
+      comb.push_back({k, 0, n, static_cast<int>(prefix_row), 2, static_cast<int>(unique_row - prefix_row)});
+    }
+  }
+
   auto longest_first = [](const Item& x, const Item& y) { return (x.pe - x.pb) > (y.pe - y.pb); };
   std::stable_sort(dec.begin(), dec.end(), longest_first);
   std::stable_sort(til.begin(), til.end(), longest_first);
   std::stable_sort(tcv.begin(), tcv.end(), longest_first);
 
   const int64_t off_seqs = 0;
-  const int64_t off_tables = round4(off_seqs + static_cast<int64_t>(num_seqs) * kRec);
+  const int64_t n_seq_records = static_cast<int64_t>(num_seqs) + static_cast<int64_t>(groups.size());
+  const int64_t off_tables = round4(off_seqs + n_seq_records * kRec);
   const int64_t off_decode = round4(off_tables + total_entries);
   const int64_t off_tile = round4(off_decode + static_cast<int64_t>(dec.size()) * kRec);
   const int64_t off_tc = round4(off_tile + static_cast<int64_t>(til.size()) * kRec);
@@ -249,6 +345,16 @@ extern "C" int ms_plan_build(int32_t num_seqs, const int32_t* flat_start, const 
     r[3] = num_cached[i] + num_new[i];
     r[4] = static_cast<int32_t>(table_offsets[i]);
     r[5] = static_cast<int32_t>(table_offsets[i + 1] - table_offsets[i]);
+  }
+  for (size_t g = 0; g < groups.size(); ++g) {
+    const Group& G = groups[g];
+    int32_t* r = out + off_seqs + (static_cast<int64_t>(num_seqs) + static_cast<int64_t>(g)) * kRec;
+    r[0] = flat_start[G.first];
+    r[1] = G.tokens;
+    r[2] = G.pages * block_size;
+    r[3] = G.pages * block_size + G.tokens;
+    r[4] = static_cast<int32_t>(table_offsets[G.first]);
+    r[5] = G.pages;
   }
   if (total_entries > 0) std::memcpy(out + off_tables, tables, sizeof(int32_t) * total_entries);
   auto put = [&](int64_t off, const std::vector<Item>& v) {
@@ -274,6 +380,7 @@ extern "C" int ms_plan_build(int32_t num_seqs, const int32_t* flat_start, const 
     r[2] = comb[k].n_q;
     r[3] = comb[k].pb;
     r[4] = comb[k].pe;
+    r[5] = comb[k].part_row;  // split stride in partial rows (0: 2 * n_q)
   }
 
   info->num_seqs = num_seqs;
@@ -286,6 +393,7 @@ extern "C" int ms_plan_build(int32_t num_seqs, const int32_t* flat_start, const 
   info->off_decode = static_cast<int32_t>(off_decode);
   info->off_tile = static_cast<int32_t>(off_tile);
   info->n_tc_items = static_cast<int32_t>(tcv.size());
+  info->n_cascade = static_cast<int32_t>(groups.size());
   info->off_tc = static_cast<int32_t>(off_tc);
   info->off_combine = static_cast<int32_t>(off_combine);
   info->total_ints = static_cast<int32_t>(total);

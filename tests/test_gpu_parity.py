@@ -17,7 +17,7 @@ import torch
 
 from golden.cases import CASES, D, EPS, H, KVH, THETA, random_inputs
 from golden_io import load_golden, make_inputs, run_oracle
-from miniserve_b200.workloads import config3, custom
+from miniserve_b200.workloads import Batch, config3, config4, custom
 from gpu_harness import bf16_ulp_diff, covered_rows, run_layer
 from oracle import attention_oracle as orc
 
@@ -117,6 +117,49 @@ def test_tensor_core_prefill_edges(rows, cuda_device: torch.device) -> None:
     for split in (0, 8):
         err = _random_case_vs_fp32(custom(rows, seed=len(rows)), 3, split, cuda_device)
         assert err <= ATOL, (split, err)
+
+
+@pytest.mark.parametrize("num_seqs", [16, 64, 512], ids=["16_rows", "64_rows", "config4"])
+def test_cascade_shared_prefix(num_seqs: int, cuda_device: torch.device) -> None:
+    """Config 4's geometry (5-token verify rows sharing a 1024-token prefix, 64..256 own tokens):
+    the prefix is attended once by the tensor-core kernel over all the rows' tokens, each row's
+    own pages by the decode kernel, and the two merged; against the fp32 oracle."""
+    batch = config4(seed=11, num_seqs=num_seqs)
+    inp = random_inputs(batch, 11)
+    got = run_layer(inp, cuda_device)
+    assert int(got["status"]) == 0
+    assert got["meta_info"].n_cascade == 1
+    rows = covered_rows(inp)
+    ref32 = _fp32_reference_out(inp, got["q_rot"], got["k_slots"], got["v_slots"])[rows]
+    err = (got["out"].cpu()[rows].float() - ref32).abs().max().item()
+    assert err <= ATOL, err
+
+
+def test_cascade_group_beside_other_rows(cuda_device: torch.device) -> None:
+    """A cascade group between a prefill chunk and unrelated decode rows, and a 15-row run that is
+    too short to form a group: every row against the fp32 oracle."""
+    g = config4(seed=12, num_seqs=20)
+    short = config4(seed=13, num_seqs=15)
+    rows = [(300, 40)] + [(c.num_new, c.num_cached) for c in g.chunks] + [(1, 900), (3, 77)]
+    rows += [(c.num_new, c.num_cached) for c in short.chunks]
+    batch = custom(rows, seed=14)
+    # custom() gives every row its own blocks; share the first 64 blocks among rows 1..20 and,
+    # separately, among the last 15 rows, as a prefix cache would.
+    chunks = list(batch.chunks)
+    for lo, hi in ((1, 21), (23, 38)):
+        prefix = list(chunks[lo].block_table[:64])
+        for i in range(lo, hi):
+            c = chunks[i]
+            chunks[i] = type(c)(c.flat_start, c.num_new, c.num_cached, prefix + list(c.block_table[64:]))
+    shared = Batch(batch.name, chunks, batch.num_blocks, 0)
+    inp = random_inputs(shared, 14)
+    got = run_layer(inp, cuda_device)
+    assert int(got["status"]) == 0
+    assert got["meta_info"].n_cascade == 1
+    rows_ = covered_rows(inp)
+    ref32 = _fp32_reference_out(inp, got["q_rot"], got["k_slots"], got["v_slots"])[rows_]
+    err = (got["out"].cpu()[rows_].float() - ref32).abs().max().item()
+    assert err <= ATOL, err
 
 
 @pytest.mark.parametrize("name", ["mixed_bf16", "prefix_verify_bf16", "prefill_bf16"])

@@ -16,7 +16,7 @@ def decode_plan(packed: np.ndarray, info):
     def recs(off: int, n: int) -> np.ndarray:
         return packed[off : off + n * REC].reshape(n, REC)
 
-    return (recs(info.off_seqs, info.num_seqs), recs(info.off_decode, info.n_decode_items),
+    return (recs(info.off_seqs, info.num_seqs + info.n_cascade), recs(info.off_decode, info.n_decode_items),
             recs(info.off_tile, info.n_tile_items), recs(info.off_tc, info.n_tc_items),
             recs(info.off_combine, info.n_combine))
 
@@ -30,6 +30,25 @@ def check_plan(chunks: list[SeqChunk], num_tokens: int, split: int = 0) -> None:
         r = seqs[i]
         assert list(r[:4]) == [c.flat_start, c.num_new, c.num_cached, c.context_len]
         assert list(flat_tables[r[4] : r[4] + r[5]]) == list(c.block_table)
+    # Cascade groups: records after the real sequences; members are consecutive decode / verify
+    # rows, contiguous in the batch, whose tables start with the group's prefix blocks.
+    cascade: dict[int, tuple[int, int]] = {}  # row -> (prefix pages, group index)
+    group_of_vseq: dict[int, tuple[int, int, int]] = {}
+    for g in range(info.n_cascade):
+        flat, tokens, cached, ctx, toff, pages = (int(x) for x in seqs[len(chunks) + g][:6])
+        assert cached == 16 * pages >= 256 and ctx == cached + tokens
+        prefix = list(flat_tables[toff : toff + pages])
+        members = [i for i, c in enumerate(chunks) if flat <= c.flat_start < flat + tokens]
+        assert len(members) >= 16 and members == list(range(members[0], members[-1] + 1))
+        assert sum(chunks[i].num_new for i in members) == tokens
+        for i in members:
+            c = chunks[i]
+            assert c.num_new <= 8 and c.num_cached >= 16 * pages
+            assert list(c.block_table[:pages]) == prefix
+            assert i not in cascade
+            cascade[i] = (pages, g)
+        group_of_vseq[len(chunks) + g] = (tokens, pages, flat)
+    vcover: dict[int, list[tuple[int, int, int, int]]] = {}
     # Every query tile's visible pages are covered exactly once by its items.  Tensor-core
     # records hold two 64-token tiles: A = (tok0, n_q), B = (fields 6, 7); unsplit chunks pair
     # groups g and G-1-g, split items keep A and B adjacent.
@@ -39,7 +58,23 @@ def check_plan(chunks: list[SeqChunk], num_tokens: int, split: int = 0) -> None:
     for kind, items in (("dec", dec), ("til", til), ("tc", tcv)):
         for it in items:
             seq, tok0, nq, pb, pe, part, tok_b, n_b = (int(x) for x in it[:8])
+            if seq >= len(chunks):
+                # a cascade group's shared prefix: adjacent 64-token tiles, pages [0, prefix)
+                tokens, pages, _ = group_of_vseq[seq]
+                assert kind == "tc" and pb == 0 and pe == pages and part >= 0 and tok0 % 128 == 0
+                assert nq == min(64, tokens - tok0) and n_b == max(0, min(64, tokens - tok0 - 64))
+                assert n_b == 0 or tok_b == tok0 + 64
+                vcover.setdefault(seq, []).append((tok0, nq + n_b, part, pe))
+                continue
             c = chunks[seq]
+            if seq in cascade:
+                # the row's own pages after the shared prefix: one unsplit decode item
+                pages, g = cascade[seq]
+                assert kind == "dec" and tok0 == 0 and nq == c.num_new and part >= 0
+                assert pb == pages and pe == -(-(c.num_cached + nq) // 16)
+                cover.setdefault((seq, tok0), []).append((pb, pe, part))
+                item_tokens[(seq, tok0)] = (nq, pe)
+                continue
             assert 0 < nq and tok0 + nq <= c.num_new
             assert 0 <= pb < pe
             if kind == "dec":
@@ -71,7 +106,26 @@ def check_plan(chunks: list[SeqChunk], num_tokens: int, split: int = 0) -> None:
             for g0 in range(0, c.num_new, 64):
                 assert tc_groups.pop((c_idx, g0)) == 1, "each 64-token group in exactly one item"
     assert not tc_groups
+    for vseq, parts in vcover.items():
+        tokens, pages, _ = group_of_vseq[vseq]
+        parts.sort()
+        assert [p[0] for p in parts] == list(range(0, tokens, 128))
+        base = parts[0][2]
+        assert all(p[2] == base + 2 * p[0] for p in parts), "prefix partial rows in token order"
+        group_of_vseq[vseq] = (tokens, pages, base)
+    assert len(vcover) == info.n_cascade
     combos = {(int(r[0]), int(r[1])): r for r in comb}
+    for key, spans in list(cover.items()):
+        if key[0] not in cascade:
+            continue
+        pages, g = cascade[key[0]]
+        _, _, base = group_of_vseq[len(chunks) + g]
+        (pb, pe, part), = spans
+        r = combos.pop(key)
+        prefix_row = base + 2 * (chunks[key[0]].flat_start - int(seqs[len(chunks) + g][0]))
+        assert int(r[2]) == chunks[key[0]].num_new and int(r[3]) == prefix_row and int(r[4]) == 2
+        assert int(r[5]) == part - prefix_row != 0, "split stride points at the row's own partials"
+        del cover[key]
     for key, spans in cover.items():
         spans = sorted(spans)
         n_tokens, pages = item_tokens[key]
@@ -82,12 +136,12 @@ def check_plan(chunks: list[SeqChunk], num_tokens: int, split: int = 0) -> None:
             assert spans[0][2] == -1 and key not in combos
         else:
             r = combos.pop(key)
-            assert int(r[2]) == n_tokens and int(r[4]) == len(spans)
+            assert int(r[2]) == n_tokens and int(r[4]) == len(spans) and int(r[5]) == 0
             parts = sorted(s[2] for s in spans)
             assert parts == [int(r[3]) + k * 2 * n_tokens for k in range(len(spans))]
     assert not combos
     for c_idx, c in enumerate(chunks):
-        if c.num_new <= 64:
+        if c.num_new <= 64 and c_idx not in cascade:
             assert (c_idx, 0) in cover
     assert info.workspace_bytes_per_kv_head == info.part_rows * 129 * 4
 
