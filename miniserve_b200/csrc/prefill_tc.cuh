@@ -55,7 +55,7 @@ struct TcCfg {
   static constexpr int kPOff = 2 * kQBytes;                // P_A, P_B
   static constexpr int kRingOff = kPOff + 2 * kQBytes;     // K/V ring
   static constexpr int kBarOff = kRingOff + kSlots * kSlotBytes;
-  static constexpr int kNumBars = 2 * kSlots + 2 + 1 + 1 + 2 + 1;
+  static constexpr int kNumBars = 2 * kSlots + 2 + 1 + 1 + 2 + 1 + 2;
   static constexpr int kSmemBytes = 1024 + kBarOff + (kNumBars + 2) * 8;
   static_assert(kSmemBytes <= 232448, "shared memory budget");
   static constexpr uint32_t kTmemCols = 512;
@@ -175,6 +175,8 @@ __global__ void __launch_bounds__(TcCfg::kThreads, 1)
   uint64_t* p_full = s_free + 1;           // both tiles' P(j) stored (and O rescaled)
   uint64_t* pv_done = p_full + 1;          // [tile]: O_t += P_t(j) V_j finished
   uint64_t* mma_drain = pv_done + 2;
+  uint64_t* q_ready = mma_drain + 1;      // both Q tiles stored in shared memory
+  uint64_t* tmem_ready = q_ready + 1;     // the TMEM allocation's address is in tmem_holder
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + TcCfg::kNumBars);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + TcCfg::kNumBars + 1);
 
@@ -220,12 +222,19 @@ __global__ void __launch_bounds__(TcCfg::kThreads, 1)
     mbar_init(s_free, 256);
     mbar_init(p_full, 256);
     mbar_init(mma_drain, 2);
+    mbar_init(q_ready, 256);
+    mbar_init(tmem_ready, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
+  // Start-up overlaps: once the barriers exist the producer streams K and V at once, while the
+  // softmax warps load Q and warp 9 allocates TMEM; only the first S waits for Q.
+  __syncthreads();
   if (warp == 9) {
     tmem_alloc(tmem_holder, TcCfg::kTmemCols);
     tmem_relinquish();
+    tc_fence_before();
+    if (lane == 0) mbar_arrive(tmem_ready);
   }
   if (warp < 8) {
     // Q tiles: thread r loads row r % 128 of tile r / 128 into the swizzled K-major layout.
@@ -234,19 +243,30 @@ __global__ void __launch_bounds__(TcCfg::kThreads, 1)
     const int tok = (t == 0 ? tok_a : tok_b) + (r >> 1);
     const __nv_bfloat16* src = a.q + static_cast<long long>(flat_start + tok) * a.q_row_stride +
                                (kvh * kGroup + (r & 1)) * kHeadDim;
-    uint8_t* qs = smem + TcCfg::kQOff + t * TcCfg::kQBytes;
+    // All 16 loads are issued before any store: a shared store through a generic pointer between
+    // them would make each load wait for the previous one (possible aliasing), 16 round trips.
+    const uint32_t qs = smem_u32(smem + TcCfg::kQOff + t * TcCfg::kQBytes);
+    uint4 v[16];
 #pragma unroll
-    for (int u = 0; u < 16; ++u) {
-      uint4 v = make_uint4(0u, 0u, 0u, 0u);
-      if (valid) v = reinterpret_cast<const uint4*>(src)[u];
-      *reinterpret_cast<uint4*>(qs + tile128_off(r, u)) = v;
-    }
+    for (int u = 0; u < 16; ++u)
+      v[u] = valid ? __ldg(reinterpret_cast<const uint4*>(src) + u) : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+    for (int u = 0; u < 16; ++u) st_shared_v4(qs + tile128_off(r, u), v[u].x, v[u].y, v[u].z, v[u].w);
     fence_proxy_async_smem();
+    mbar_arrive(q_ready);
   }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_holder;
+  uint32_t tmem = 0;
+  bool tmem_ok = true;
+  if (warp != 8) {
+    tmem_ok = mbar_wait_fast(tmem_ready, 0, abort_flag);
+    tc_fence_after();
+    if (tmem_ok) {
+      tmem = *tmem_holder;
+    } else if (lane == 0) {
+      atomicOr(&g_status_word, kErrTimeout);
+      *abort_flag = 1;
+    }
+  }
 
   if (warp == 8) {
     // ---------------- TMA producer ----------------
@@ -308,6 +328,8 @@ __global__ void __launch_bounds__(TcCfg::kThreads, 1)
         }
       }
     }
+  } else if (!tmem_ok) {
+    // The TMEM address never became visible (the status word says why): no MMA or softmax work.
   } else if (warp == 9 || warp == 10) {
     // ---------------- MMA issuers: warp 9 issues every S = Q K^T, warp 10 every O += P V ------
     // Two issuing threads, two independent MMA streams (different TMEM columns and operands): the
@@ -332,7 +354,8 @@ __global__ void __launch_bounds__(TcCfg::kThreads, 1)
       constexpr uint32_t kSlot16 = TcCfg::kSlotBytes >> 4;
       if (!is_pv) {
         // S_t(j) = Q_t K_j^T into tile t's S columns, as soon as both tiles hold S(j-1) in
-        // registers and K_j has landed.
+        // registers and K_j has landed (and, for S(0), Q is stored).
+        ok = nblk == 0 || mbar_wait_mma(q_ready, 0, abort_flag);
         for (int j = 0; ok && j < nblk; ++j) {
           if (!(ok = wait_slot(pos_k(j)) && (j == 0 || mbar_wait_mma(s_free, (j - 1) & 1,
                                                                       abort_flag))))
