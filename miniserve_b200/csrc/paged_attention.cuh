@@ -179,23 +179,41 @@ __global__ void __launch_bounds__(AttnCfg<kMode, kConsumerWarps, kStages>::kThre
     fence_barrier_init();
   }
 
-  // Query tile -> shared memory, swizzled like a page: [16-row group][d/64][row][d%64].
+  // The producer starts streaming pages as soon as the barriers exist; the consumer warps load
+  // the query tile meanwhile and synchronise among themselves (named barrier 1).
+  __syncthreads();
   if (warp < kConsumerWarps) {
-    const int nthreads = kConsumerWarps * 32;
-    for (int c = threadIdx.x; c < Cfg::kRows * 16; c += nthreads) {
+    // Query tile -> shared memory, swizzled like a page: [16-row group][d/64][row][d%64].  All of
+    // a thread's loads are issued before its shared stores (a store between them would make each
+    // load wait for the previous one).
+    constexpr int kPer = Cfg::kRows * 16 / (kConsumerWarps * 32);
+    static_assert(Cfg::kRows * 16 % (kConsumerWarps * 32) == 0, "query chunks per thread");
+    uint4 v[kPer];
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+      const int c = threadIdx.x + k * kConsumerWarps * 32;
       const int r = c >> 4;
       const int d = (c & 15) * 8;
       const int tok = r >> 1;
-      uint4 v = make_uint4(0u, 0u, 0u, 0u);
-      if (tok < n_q) {
-        const __nv_bfloat16* src = a.q + static_cast<long long>(flat_start + tok0 + tok) * a.q_row_stride +
-                                   (kvh * kGroup + (r & 1)) * kHeadDim + d;
-        v = *reinterpret_cast<const uint4*>(src);
-      }
-      *reinterpret_cast<uint4*>(qtile + (r >> 4) * (16 * kHeadDim * 2) + swz_off(r & 15, d, 16)) = v;
+      v[k] = make_uint4(0u, 0u, 0u, 0u);
+      if (tok < n_q)
+        v[k] = __ldg(reinterpret_cast<const uint4*>(
+            a.q + static_cast<long long>(flat_start + tok0 + tok) * a.q_row_stride +
+            (kvh * kGroup + (r & 1)) * kHeadDim + d));
     }
+    const uint32_t qbase_s = smem_u32(qtile);
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+      const int c = threadIdx.x + k * kConsumerWarps * 32;
+      const int r = c >> 4;
+      const int d = (c & 15) * 8;
+      asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(
+                       qbase_s + (r >> 4) * (16 * kHeadDim * 2) + swz_off(r & 15, d, 16)),
+                   "r"(v[k].x), "r"(v[k].y), "r"(v[k].z), "r"(v[k].w)
+                   : "memory");
+    }
+    asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
   }
-  __syncthreads();
 
   if (warp == kConsumerWarps) {
     // ---------------- producer warp ----------------
@@ -281,7 +299,7 @@ __global__ void __launch_bounds__(AttnCfg<kMode, kConsumerWarps, kStages>::kThre
   for (int j = jstart; j < npages; j += jstep) {
     const int s = j % kStages;
     // Leave the loop only as a whole warp: the tensor-core ops below are warp-collective.
-    const bool ok = __all_sync(0xffffffffu, *abort_flag == 0 && mbar_wait(&full[s], (j / kStages) & 1));
+    const bool ok = __all_sync(0xffffffffu, mbar_wait_fast(&full[s], (j / kStages) & 1, abort_flag));
     if (!ok) {
       if (lane == 0) {
         atomicOr(&g_status_word, kErrTimeout);
