@@ -263,13 +263,35 @@ def run_ours(args: argparse.Namespace, rank: int, world: int, device: torch.devi
     # ---- e2e: through the public API with host buffers ----
     qkv_host = qkv_all.cpu().pin_memory()
     out_host = torch.empty(LAYERS, t, H, D, dtype=torch.bfloat16).pin_memory()
-    pos_host = torch.from_numpy(batch.positions).pin_memory()
-    slot_host = torch.from_numpy(batch.slots).pin_memory()
     qkv_dev = torch.empty_like(qkv_all)
 
+    # Host preparation each step, as an engine runs it: positions and slot mappings from the
+    # block tables (ms_prepare_step, into alternating pinned buffers), then the plan.
+    from miniserve_b200.attention import prepare_arrays
+
+    n_seq = len(batch.chunks)
+    new_np = np.fromiter((c.num_new for c in batch.chunks), dtype=np.int32, count=n_seq)
+    cached_np = np.fromiter((c.num_cached for c in batch.chunks), dtype=np.int32, count=n_seq)
+    offsets_np = np.zeros(n_seq + 1, dtype=np.int64)
+    np.cumsum([len(c.block_table) for c in batch.chunks], out=offsets_np[1:])
+    tables_np = np.concatenate([np.asarray(c.block_table, dtype=np.int32) for c in batch.chunks])
+    pos_bufs = [torch.empty(t, dtype=torch.int64).pin_memory() for _ in range(2)]
+    slot_bufs = [torch.empty(t, dtype=torch.int64).pin_memory() for _ in range(2)]
+    copies_done: list = [None, None]
+    step_no = [0]
+
     def e2e_step() -> None:
-        slots_d = slot_host.to(device, non_blocking=True)
-        pos_d = pos_host.to(device, non_blocking=True)
+        k = step_no[0] & 1
+        step_no[0] += 1
+        if copies_done[k] is not None:
+            copies_done[k].synchronize()  # the copy that read this buffer two steps ago is done
+        prepare_arrays(new_np, cached_np, offsets_np, tables_np, pos_bufs[k].numpy(),
+                       slot_bufs[k].numpy())
+        slots_d = slot_bufs[k].to(device, non_blocking=True)
+        pos_d = pos_bufs[k].to(device, non_blocking=True)
+        done = torch.cuda.Event()
+        done.record(stream)
+        copies_done[k] = done
         m = build_attention_metadata(batch.chunks, slots_d, 16, pages_per_split=args.pages_per_split)
         qkv_dev.copy_(qkv_host, non_blocking=True)
         c, s = cos_t[pos_d], sin_t[pos_d]
@@ -292,7 +314,7 @@ def run_ours(args: argparse.Namespace, rank: int, world: int, device: torch.devi
     e_stop.record(stream)
     torch.cuda.synchronize(device)
     e2e_ms = e_start.elapsed_time(e_stop)
-    h2d = qkv_host.numel() * 2 + pos_host.numel() * 8 + slot_host.numel() * 8 + int(info.total_ints) * 4
+    h2d = qkv_host.numel() * 2 + pos_bufs[0].numel() * 8 + slot_bufs[0].numel() * 8 + int(info.total_ints) * 4
     d2h = out_host.numel() * 2
 
     attn_bytes, a_bytes, attn_flops = attention_bytes(batch)
@@ -506,7 +528,10 @@ def main() -> None:
             },
             "cpu_baseline": cpu,
             "e2e": {"value": tokens_all / (e2e_per_step * 1e-3), "unit": "tok/s",
-                    "h2d_bytes_per_step": r["h2d"], "d2h_bytes_per_step": r["d2h"]},
+                    "h2d_bytes_per_step": r["h2d"], "d2h_bytes_per_step": r["d2h"],
+                    "host_work_per_step": "ms_prepare_step (positions, slots) + ms_plan_build "
+                                          "+ one plan upload; qkv of all layers in, outputs of "
+                                          "all layers out"},
             "gpu_launches": r["launches_per_step"] * args.steps,
             "clocks": r["clocks"],
             "plan": r["plan"],

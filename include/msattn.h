@@ -101,6 +101,20 @@ MS_API int ms_plan_build(int32_t num_seqs, const int32_t* flat_start, const int3
                   int32_t num_tokens, int32_t block_size, int32_t num_sms,
                   int32_t pages_per_split, int32_t* out, int64_t out_capacity, MsPlanInfo* info);
 
+/* Runner step preparation (host only).  Replaces the attention inputs of ModelRunner.prepare
+ * (src/miniserve/runner/model_runner.py:162-205), which walks every scheduled token in Python:
+ * sequence i schedules num_new[i] tokens after num_cached[i] computed ones, with block table
+ * tables[table_offsets[i] .. table_offsets[i+1]).  Writes flat_start[i] (its first row in the
+ * flat batch), and for its tokens, in flat-batch order, positions[t] = num_cached[i] + k and
+ * slot_mapping[t] = table[p / block_size] * block_size + p % block_size (the reference's slot
+ * formula, model_runner.py:188), and *num_tokens.  The outputs feed ms_plan_build and
+ * ms_qk_norm_rope_scatter directly.  Errors: MS_ERR_ARG (bad sizes), MS_ERR_PLAN (a table
+ * shorter than its context), MS_ERR_CAPACITY (more tokens than capacity_tokens). */
+MS_API int ms_prepare_step(int32_t num_seqs, const int32_t* num_new, const int32_t* num_cached,
+                    const int64_t* table_offsets, const int32_t* tables, int32_t block_size,
+                    int32_t* flat_start, int64_t* positions, int64_t* slot_mapping,
+                    int64_t capacity_tokens, int32_t* num_tokens);
+
 /* ---- Kernel A: q/k RMSNorm + RoPE + K/V scatter ----------------------------------------------
  * Replaces, for one layer, qwen3.py:94-98 (split, q_norm, k_norm, apply_rope) and the K/V
  * index_copy_ at backends.py:159-160.  qkv is the fused projection output [T, (H+2*KVH)*128];

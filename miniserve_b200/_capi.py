@@ -32,6 +32,7 @@ EXPORTED = (
     "ms_device_status",
     "ms_plan_capacity",
     "ms_plan_build",
+    "ms_prepare_step",
     "ms_qk_norm_rope_scatter",
     "ms_kv_scatter",
     "ms_paged_attention",
@@ -76,6 +77,7 @@ _SIGNATURES = {
         C.c_int,
         [_I32, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _P, _I64, C.POINTER(MsPlanInfo)],
     ),
+    "ms_prepare_step": (C.c_int, [_I32, _P, _P, _P, _P, _I32, _P, _P, _P, _I64, _P]),
     "ms_qk_norm_rope_scatter": (
         C.c_int,
         [_P, _I64, _I32, _I32, _I32, _P, _P, C.c_float, _P, _P, _I64, _P, _I64, _P, _P, _I64,

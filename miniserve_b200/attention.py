@@ -111,6 +111,65 @@ def plan_batch(
     return out[: info.total_ints], info
 
 
+def prepare_arrays(num_new: np.ndarray, num_cached: np.ndarray, table_offsets: np.ndarray,
+                   tables: np.ndarray, positions_out: np.ndarray, slots_out: np.ndarray
+                   ) -> tuple[np.ndarray, int]:
+    """``ms_prepare_step`` over CSR arrays (int32 num_new / num_cached / tables, int64
+    table_offsets of length n + 1) into caller buffers (contiguous int64, e.g. pinned host
+    memory).  Returns ``(flat_start int32, num_tokens)``."""
+    lib = _capi.load()
+    n = int(num_new.shape[0])
+    for arr, dt, name in ((num_new, np.int32, "num_new"), (num_cached, np.int32, "num_cached"),
+                          (table_offsets, np.int64, "table_offsets"), (tables, np.int32, "tables"),
+                          (positions_out, np.int64, "positions_out"),
+                          (slots_out, np.int64, "slots_out")):
+        if arr.dtype != dt or not arr.flags.c_contiguous:
+            raise ValueError(f"{name} must be a contiguous {np.dtype(dt).name} array")
+    if num_cached.shape[0] != n or table_offsets.shape[0] != n + 1:
+        raise ValueError("num_cached / table_offsets do not match num_new")
+    tokens = int(num_new.sum(dtype=np.int64))
+    if positions_out.shape[0] < tokens or slots_out.shape[0] < tokens:
+        raise ValueError(f"positions_out / slots_out must be contiguous int64 arrays of >= {tokens} "
+                         "elements")
+    flat = np.empty(n, dtype=np.int32)
+    got = C.c_int32(0)
+    rc = lib.ms_prepare_step(
+        n, num_new.ctypes.data, num_cached.ctypes.data, table_offsets.ctypes.data,
+        tables.ctypes.data if tables.size else None, BLOCK_SIZE, flat.ctypes.data,
+        positions_out.ctypes.data, slots_out.ctypes.data,
+        min(positions_out.shape[0], slots_out.shape[0]), C.byref(got))
+    _capi.check(rc, "prepare_step")
+    return flat, got.value
+
+
+def prepare_step(
+    scheduled: list[tuple[int, int, list[int]]],
+    *,
+    positions_out: np.ndarray | None = None,
+    slots_out: np.ndarray | None = None,
+) -> tuple[list[SeqChunk], np.ndarray, np.ndarray]:
+    """The attention inputs of ``ModelRunner.prepare`` (model_runner.py:162-205) in one native
+    pass (``ms_prepare_step``).  ``scheduled`` holds ``(num_new, num_cached, block_table)`` per
+    sequence in batch order; returns ``(chunks, positions, slot_mapping)`` with int64 positions
+    and slots (``table[p // 16] * 16 + p % 16``) in flat-batch order.  Optional ``*_out`` arrays
+    (int64, e.g. views of pinned host tensors) receive the results without new allocations."""
+    n = len(scheduled)
+    new = np.fromiter((s[0] for s in scheduled), dtype=np.int32, count=n)
+    cached = np.fromiter((s[1] for s in scheduled), dtype=np.int32, count=n)
+    lens = np.fromiter((len(s[2]) for s in scheduled), dtype=np.int64, count=n)
+    offsets = np.zeros(n + 1, dtype=np.int64)
+    np.cumsum(lens, out=offsets[1:])
+    total = int(offsets[-1])
+    tables = np.fromiter(chain.from_iterable(s[2] for s in scheduled), dtype=np.int32, count=total)
+    tokens = int(new.sum(dtype=np.int64))
+    positions = positions_out if positions_out is not None else np.empty(tokens, dtype=np.int64)
+    slots = slots_out if slots_out is not None else np.empty(tokens, dtype=np.int64)
+    flat, got = prepare_arrays(new, cached, offsets, tables, positions, slots)
+    chunks = [SeqChunk(int(flat[i]), int(new[i]), int(cached[i]), list(scheduled[i][2]))
+              for i in range(n)]
+    return chunks, positions[:got], slots[:got]
+
+
 def build_attention_metadata(
     chunks: list[SeqChunk],
     slot_mapping: Tensor,

@@ -405,3 +405,53 @@ extern "C" int ms_plan_build(int32_t num_seqs, const int32_t* flat_start, const 
   info->workspace_bytes_per_kv_head = part_rows * (128 + 1) * 4;
   return MS_OK;
 }
+
+extern "C" int ms_prepare_step(int32_t num_seqs, const int32_t* num_new, const int32_t* num_cached,
+                               const int64_t* table_offsets, const int32_t* tables,
+                               int32_t block_size, int32_t* flat_start, int64_t* positions,
+                               int64_t* slot_mapping, int64_t capacity_tokens,
+                               int32_t* num_tokens) {
+  if (num_tokens == nullptr || num_seqs < 0 || block_size <= 0 || capacity_tokens < 0) {
+    ms_host::set_error("ms_prepare_step: bad sizes");
+    return MS_ERR_ARG;
+  }
+  *num_tokens = 0;
+  if (num_seqs > 0 && (num_new == nullptr || num_cached == nullptr || table_offsets == nullptr ||
+                       flat_start == nullptr)) {
+    ms_host::set_error("ms_prepare_step: null batch arrays");
+    return MS_ERR_ARG;
+  }
+  int64_t flat = 0;
+  for (int i = 0; i < num_seqs; ++i) {
+    const int64_t n = num_new[i], c = num_cached[i];
+    const int64_t off = table_offsets[i], tlen = table_offsets[i + 1] - off;
+    if (n < 1 || c < 0 || tlen < 0 || off < 0) {
+      ms_host::set_error("ms_prepare_step: sequence " + std::to_string(i) +
+                         " has an invalid num_new/num_cached/table");
+      return MS_ERR_ARG;
+    }
+    if (tlen * block_size < c + n) {
+      ms_host::set_error("ms_prepare_step: sequence " + std::to_string(i) + " needs " +
+                         std::to_string((c + n + block_size - 1) / block_size) +
+                         " blocks but its table has " + std::to_string(tlen));
+      return MS_ERR_PLAN;
+    }
+    if (flat + n > capacity_tokens || flat + n >= (int64_t(1) << 31)) {
+      ms_host::set_error("ms_prepare_step: more than " + std::to_string(capacity_tokens) +
+                         " tokens scheduled");
+      return MS_ERR_CAPACITY;
+    }
+    if (n > 0 && (positions == nullptr || slot_mapping == nullptr || tables == nullptr)) {
+      ms_host::set_error("ms_prepare_step: null output arrays");
+      return MS_ERR_ARG;
+    }
+    flat_start[i] = static_cast<int32_t>(flat);
+    const int32_t* table = tables + off;
+    for (int64_t p = c; p < c + n; ++p, ++flat) {
+      positions[flat] = p;
+      slot_mapping[flat] = static_cast<int64_t>(table[p / block_size]) * block_size + p % block_size;
+    }
+  }
+  *num_tokens = static_cast<int32_t>(flat);
+  return MS_OK;
+}

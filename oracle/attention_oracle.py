@@ -129,6 +129,25 @@ def slots_for(chunk: SeqChunk, block_size: int) -> list[int]:
     ]
 
 
+def prepare_step(scheduled: list[tuple[int, int, list[int]]], block_size: int
+                 ) -> tuple[list[SeqChunk], list[int], list[int]]:
+    """The attention inputs of ModelRunner.prepare (src/miniserve/runner/model_runner.py:
+    162-205): flatten the scheduled sequences' tokens in batch order; each token's position in
+    its own sequence (:185) and slot ``table[p // bs] * bs + p % bs`` (:187-188); one SeqChunk
+    per sequence at its flat offset (:189).  ``scheduled`` holds ``(num_new, num_cached,
+    block_table)``; token ids, logits rows and sampling are outside the attention path."""
+    positions: list[int] = []
+    slots: list[int] = []
+    chunks: list[SeqChunk] = []
+    for n, start, table in scheduled:
+        flat = len(positions)
+        positions.extend(range(start, start + n))
+        slots.extend(table[p // block_size] * block_size + p % block_size
+                     for p in range(start, start + n))
+        chunks.append(SeqChunk(flat, n, start, list(table)))
+    return chunks, positions, slots
+
+
 def _page_lookup(tables: Tensor, length: int, block_size: int) -> Tensor:
     """Slot of every context position 0..length-1 through a table (backends.py:74-77)."""
     pos = torch.arange(length, device=tables.device)
