@@ -384,14 +384,8 @@ extern "C" int ms_paged_attention(const void* q, int64_t q_row_stride, void* out
   a.ws_lse = ws != nullptr ? ws + plan->part_rows * num_kv_heads * ms::kHeadDim : nullptr;
   a.scale_log2 = scale * 1.4426950408889634f;
 
-  if (plan->n_decode_items > 0) {
-    a.items = plan_dev + plan->off_decode;
-    a.n_items = plan->n_decode_items;
-    ms::paged_attn_kernel<0, kDecodeWarps, kDecodeStages>
-        <<<plan->n_decode_items * num_kv_heads, DecodeCfg::kThreads, DecodeCfg::kSmemBytes, s>>>(map, a);
-    const cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return cuda_fail("paged_attn decode launch", e);
-  }
+  // The tensor-core kernel runs first: cascade rows' decode items merge the shared-prefix
+  // partials it writes.
   if (plan->n_tc_items > 0) {
     a.items = plan_dev + plan->off_tc;
     a.n_items = plan->n_tc_items;
@@ -399,6 +393,14 @@ extern "C" int ms_paged_attention(const void* q, int64_t q_row_stride, void* out
                             ms::TcCfg::kSmemBytes, s>>>(kmap, vmap, a);
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail("prefill_tc launch", e);
+  }
+  if (plan->n_decode_items > 0) {
+    a.items = plan_dev + plan->off_decode;
+    a.n_items = plan->n_decode_items;
+    ms::paged_attn_kernel<0, kDecodeWarps, kDecodeStages>
+        <<<plan->n_decode_items * num_kv_heads, DecodeCfg::kThreads, DecodeCfg::kSmemBytes, s>>>(map, a);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail("paged_attn decode launch", e);
   }
   if (plan->n_tile_items > 0) {
     a.items = plan_dev + plan->off_tile;

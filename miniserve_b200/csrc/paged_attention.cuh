@@ -165,6 +165,9 @@ __global__ void __launch_bounds__(AttnCfg<kMode, kConsumerWarps, kStages>::kThre
   const int* it = a.items + static_cast<long long>(item_idx) * kRec;
   const int seq = it[0], tok0 = it[1], n_q = it[2], page_begin = it[3], page_end = it[4],
             part_row = it[5];
+  // Decode items of cascade rows (field 7 = 1) merge the shared-prefix partial rows starting at
+  // field 6 into their output.
+  const int merge_row = (kMode == 0 && it[7] == 1) ? it[6] : -1;
   const int* sr = a.seqs + static_cast<long long>(seq) * kRec;
   const int flat_start = sr[0], num_cached = sr[2], table_off = sr[4];
   const int npages = page_end - page_begin;
@@ -376,9 +379,37 @@ __global__ void __launch_bounds__(AttnCfg<kMode, kConsumerWarps, kStages>::kThre
       if (part_row < 0) {
         __nv_bfloat16* dst = a.out + static_cast<long long>(flat_start + tok0 + tok) * a.out_row_stride +
                              head * kHeadDim + dc;
+        float scale_u = invL;  // weight of this item's own (unnormalised) accumulator
+        float wp = 0.f;        // weight of the merged shared-prefix partial
+        const float* op = nullptr;
+        if (merge_row >= 0) {
+          // Cascade row: merge the shared-prefix partial (normalised O and log2-sum-exp) that the
+          // tensor-core kernel wrote before this launch: out = (acc 2^(mx-M) + O_p L_p') / (...).
+          const long long prow = static_cast<long long>(merge_row + r) * a.num_kv + kvh;
+          const float lse_p = a.ws_lse[prow];
+          const float lse_u = L > 0.f ? mx + __log2f(L) : -INFINITY;
+          const float M = fmaxf(lse_u, lse_p);
+          const float wu = lse_u == -INFINITY ? 0.f : fast_exp2(lse_u - M);
+          wp = lse_p == -INFINITY ? 0.f : fast_exp2(lse_p - M);
+          const float inv = wu + wp > 0.f ? 1.f / (wu + wp) : 0.f;
+          scale_u = invL * wu * inv;
+          wp *= inv;
+          op = a.ws_o + prow * kHeadDim + dc;
+        }
+        if (op != nullptr) {
+#pragma unroll
+          for (int i = 0; i < 16; i += 4) {
+            const float4 pv = *reinterpret_cast<const float4*>(op + i);
+            acc[i] = acc[i] * scale_u + pv.x * wp;
+            acc[i + 1] = acc[i + 1] * scale_u + pv.y * wp;
+            acc[i + 2] = acc[i + 2] * scale_u + pv.z * wp;
+            acc[i + 3] = acc[i + 3] * scale_u + pv.w * wp;
+          }
+          scale_u = 1.f;
+        }
         uint32_t pk[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) pk[i] = pack_bf16(acc[2 * i] * invL, acc[2 * i + 1] * invL);
+        for (int i = 0; i < 8; ++i) pk[i] = pack_bf16(acc[2 * i] * scale_u, acc[2 * i + 1] * scale_u);
         reinterpret_cast<uint4*>(dst)[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
         reinterpret_cast<uint4*>(dst)[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
       } else {

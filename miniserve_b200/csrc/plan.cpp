@@ -18,8 +18,8 @@
 //   * a run of >= 16 consecutive decode / verify rows, contiguous in the batch, whose block tables
 //     begin with the same >= 16 cached blocks is a cascade group: the shared prefix is attended
 //     once by tensor-core items over all the group's query tokens (a virtual sequence record
-//     after the real ones), each row's remaining pages by an unsplit decode item, and a two-way
-//     combine merges them.
+//     after the real ones, run first), and each row's remaining pages by an unsplit decode item
+//     whose epilogue merges the prefix partials.
 // Items are ordered longest first so the hardware block scheduler fills the tail with short ones.
 #include <algorithm>
 #include <cstdint>
@@ -60,7 +60,9 @@ constexpr int kCascadeMinPages = 16;
 
 struct Item {
   int seq, tok0, n_q, pb, pe, part_row;
-  int tok_b = 0, n_b = 0;  // tensor-core items: tile B's first token and token count
+  // Fields 6 and 7.  Tensor-core items: tile B's first token and token count.  Decode items of
+  // cascade rows: the first shared-prefix partial row to merge, and 1.
+  int tok_b = 0, n_b = 0;
 };
 
 int64_t round4(int64_t x) { return (x + 3) & ~int64_t(3); }
@@ -286,11 +288,12 @@ extern "C" int ms_plan_build(int32_t num_seqs, const int32_t* flat_start, const 
   // Cascade groups.  The shared prefix is attended once by tensor-core items over a virtual
   // sequence (record num_seqs + g): the group's query tokens, contiguous in the batch, with the
   // prefix as their cached context, so every prefix key is visible to every query.  Its items
-  // write partial rows for all the group's tokens; each row then attends its own pages after the
-  // prefix with an unsplit decode item, and a two-way combine (split stride in field 5) merges.
+  // write partial rows for all the group's tokens (the tensor-core kernel runs first); each row
+  // then attends its own pages after the prefix with an unsplit decode item whose epilogue
+  // merges the row's prefix partials (fields 6 and 7: first partial row, 1).
   for (size_t g = 0; g < groups.size(); ++g) {
     const Group& G = groups[g];
-    if (part_rows + 4 * static_cast<int64_t>(G.tokens) >= (int64_t(1) << 31)) {
+    if (part_rows + 2 * static_cast<int64_t>(G.tokens) >= (int64_t(1) << 31)) {
       ms_host::set_error("ms_plan_build: too many partial rows");
       return MS_ERR_PLAN;
     }
@@ -306,11 +309,9 @@ extern "C" int ms_plan_build(int32_t num_seqs, const int32_t* flat_start, const 
     for (int k = G.first; k < G.last; ++k) {
       const int n = num_new[k];
       const int pages = static_cast<int>((static_cast<int64_t>(num_cached[k]) + n + block_size - 1) / block_size);
-      const int64_t unique_row = part_rows;
-      part_rows += 2 * n;
-      dec.push_back({k, 0, n, G.pages, pages, static_cast<int>(unique_row)});
       const int64_t prefix_row = prefix_base + 2 * (static_cast<int64_t>(flat_start[k]) - flat_start[G.first]);
-      comb.push_back({k, 0, n, static_cast<int>(prefix_row), 2, static_cast<int>(unique_row - prefix_row)});
+      // Own pages, merged with the prefix partial in the decode kernel's epilogue (field 7 = 1).
+      dec.push_back({k, 0, n, G.pages, pages, -1, static_cast<int>(prefix_row), 1});
     }
   }
 

@@ -68,11 +68,12 @@ def check_plan(chunks: list[SeqChunk], num_tokens: int, split: int = 0) -> None:
                 continue
             c = chunks[seq]
             if seq in cascade:
-                # the row's own pages after the shared prefix: one unsplit decode item
+                # the row's own pages after the shared prefix: one unsplit decode item that
+                # merges the row's prefix partials (fields 6, 7) into its output
                 pages, g = cascade[seq]
-                assert kind == "dec" and tok0 == 0 and nq == c.num_new and part >= 0
-                assert pb == pages and pe == -(-(c.num_cached + nq) // 16)
-                cover.setdefault((seq, tok0), []).append((pb, pe, part))
+                assert kind == "dec" and tok0 == 0 and nq == c.num_new and part == -1
+                assert pb == pages and pe == -(-(c.num_cached + nq) // 16) and n_b == 1
+                cover.setdefault((seq, tok0), []).append((pb, pe, tok_b))
                 item_tokens[(seq, tok0)] = (nq, pe)
                 continue
             assert 0 < nq and tok0 + nq <= c.num_new
@@ -120,11 +121,10 @@ def check_plan(chunks: list[SeqChunk], num_tokens: int, split: int = 0) -> None:
             continue
         pages, g = cascade[key[0]]
         _, _, base = group_of_vseq[len(chunks) + g]
-        (pb, pe, part), = spans
-        r = combos.pop(key)
+        (pb, pe, merge_row), = spans
+        assert key not in combos, "cascade rows merge in the decode kernel, no combine record"
         prefix_row = base + 2 * (chunks[key[0]].flat_start - int(seqs[len(chunks) + g][0]))
-        assert int(r[2]) == chunks[key[0]].num_new and int(r[3]) == prefix_row and int(r[4]) == 2
-        assert int(r[5]) == part - prefix_row != 0, "split stride points at the row's own partials"
+        assert merge_row == prefix_row
         del cover[key]
     for key, spans in cover.items():
         spans = sorted(spans)
