@@ -47,7 +47,6 @@ struct TcCfg {
   static constexpr int kThreads = 352;
   static constexpr int kSlots = 3;          // K/V ring slots (one 128-key K or V block each)
   static constexpr int kTileTokens = 64;    // query tokens per 128-row tile
-  static constexpr int kItemTokens = 128;   // query tokens per work item (two tiles)
   static constexpr int kBlockKeys = 128;
   static constexpr int kQBytes = 32768;     // one tile: [2 halves][128 rows][64]
   static constexpr int kSlotBytes = 32768;  // one 128-key K (or V) block
