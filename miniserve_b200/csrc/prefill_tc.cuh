@@ -23,9 +23,9 @@
 //               unit fills with zeros.
 //   warps 9, 10 MMA issuers (warp 9 also allocates the 512 TMEM columns); every MMA takes both
 //               operands from shared memory, P included:
-//                 warp 9:  S_t(j) = Q_t K_j^T  (M=128, N=128, K=128) once both tiles hold S(j-1)
+//                 warp 9:  S_t(j) = Q_t K_j^T  (M=128, N=128, K=128) once tile t holds S_t(j-1)
 //                          in registers
-//                 warp 10: O_t += P_t(j) V_j   (M=128, N=128, K=128) once both P(j) are stored
+//                 warp 10: O_t += P_t(j) V_j   (M=128, N=128, K=128) once P_t(j) is stored
 //               One thread's MMA issue queue is shallow, so a wait in a single issuer idles the
 //               tensor core; with two independent streams one keeps it busy while the other waits.
 //               The scores of the next block are ready before the softmax needs them and the
@@ -54,7 +54,7 @@ struct TcCfg {
   static constexpr int kPOff = 2 * kQBytes;                // P_A, P_B
   static constexpr int kRingOff = kPOff + 2 * kQBytes;     // K/V ring
   static constexpr int kBarOff = kRingOff + kSlots * kSlotBytes;
-  static constexpr int kNumBars = 2 * kSlots + 2 + 1 + 1 + 2 + 1 + 2;
+  static constexpr int kNumBars = 2 * kSlots + 2 + 2 + 2 + 2 + 1 + 2;
   static constexpr int kSmemBytes = 1024 + kBarOff + (kNumBars + 2) * 8;
   static_assert(kSmemBytes <= 232448, "shared memory budget");
   static constexpr uint32_t kTmemCols = 512;
@@ -171,9 +171,9 @@ __global__ void __launch_bounds__(TcCfg::kThreads, 1)
   uint64_t* slot_full = bars;              // [NS]
   uint64_t* slot_empty = slot_full + NS;   // [NS]
   uint64_t* s_full = slot_empty + NS;      // [tile]: S_t(j) computed
-  uint64_t* s_free = s_full + 2;           // both tiles' S(j) read into registers
-  uint64_t* p_full = s_free + 1;           // both tiles' P(j) stored (and O rescaled)
-  uint64_t* pv_done = p_full + 1;          // [tile]: O_t += P_t(j) V_j finished
+  uint64_t* s_free = s_full + 2;           // [tile]: S_t(j) read into registers
+  uint64_t* p_full = s_free + 2;           // [tile]: P_t(j) stored (and O_t rescaled)
+  uint64_t* pv_done = p_full + 2;          // [tile]: O_t += P_t(j) V_j finished
   uint64_t* mma_drain = pv_done + 2;
   uint64_t* q_ready = mma_drain + 1;      // both Q tiles stored in shared memory
   uint64_t* tmem_ready = q_ready + 1;     // the TMEM allocation's address is in tmem_holder
@@ -216,11 +216,10 @@ __global__ void __launch_bounds__(TcCfg::kThreads, 1)
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(&s_full[t], 1);
+      mbar_init(&s_free[t], 128);
+      mbar_init(&p_full[t], 128);
       mbar_init(&pv_done[t], 1);
     }
-    // One phase per block for both tiles (see the softmax's arrive count).
-    mbar_init(s_free, 256);
-    mbar_init(p_full, 256);
     mbar_init(mma_drain, 2);
     mbar_init(q_ready, 256);
     mbar_init(tmem_ready, 1);
@@ -353,17 +352,17 @@ __global__ void __launch_bounds__(TcCfg::kThreads, 1)
       const uint64_t dv = umma_smem_desc_sw128(ring, 2048, 1024);  // [page][half][16 keys][64]
       constexpr uint32_t kSlot16 = TcCfg::kSlotBytes >> 4;
       if (!is_pv) {
-        // S_t(j) = Q_t K_j^T into tile t's S columns, as soon as both tiles hold S(j-1) in
-        // registers and K_j has landed (and, for S(0), Q is stored).
+        // S_t(j) = Q_t K_j^T into tile t's S columns, as soon as tile t holds S_t(j-1) in
+        // registers and K_j has landed (and, for S(0), Q is stored).  The tiles are not coupled:
+        // each goes as soon as its own softmax has released its S columns.
         ok = nblk == 0 || mbar_wait_mma(q_ready, 0, abort_flag);
         for (int j = 0; ok && j < nblk; ++j) {
-          if (!(ok = wait_slot(pos_k(j)) && (j == 0 || mbar_wait_mma(s_free, (j - 1) & 1,
-                                                                      abort_flag))))
-            break;
-          tc_fence_after();
+          if (!(ok = wait_slot(pos_k(j)))) break;
           const uint64_t kd = dk + (pos_k(j) % NS) * kSlot16;
-          for (int t = 0; t < 2; ++t) {
+          for (int t = 0; ok && t < 2; ++t) {
             if (j < nblk_t[t]) {
+              if (j > 0 && !(ok = mbar_wait_mma(&s_free[t], (j - 1) & 1, abort_flag))) break;
+              tc_fence_after();
               const uint64_t qd = dq + t * (TcCfg::kQBytes >> 4);
 #pragma unroll
               for (int kk = 0; kk < 8; ++kk) {
@@ -373,16 +372,18 @@ __global__ void __launch_bounds__(TcCfg::kThreads, 1)
               umma_commit(&s_full[t]);
             }
           }
+          if (!ok) break;
           umma_commit(&slot_empty[pos_k(j) % NS]);
         }
       } else {
-        // O_t += P_t(j) V_j once both tiles' P(j) are stored and V_j has landed.
+        // O_t += P_t(j) V_j once tile t's P(j) is stored and V_j has landed.
         for (int j = 0; ok && j < nblk; ++j) {
-          if (!(ok = wait_slot(pos_v(j)) && mbar_wait_mma(p_full, j & 1, abort_flag))) break;
-          tc_fence_after();
+          if (!(ok = wait_slot(pos_v(j)))) break;
           const uint64_t vd = dv + (pos_v(j) % NS) * kSlot16;
-          for (int t = 0; t < 2; ++t) {
+          for (int t = 0; ok && t < 2; ++t) {
             if (j < nblk_t[t]) {
+              if (!(ok = mbar_wait_mma(&p_full[t], j & 1, abort_flag))) break;
+              tc_fence_after();
 #pragma unroll
               for (int kk = 0; kk < 8; ++kk)
                 umma_bf16_ss(tmem + TcCfg::kOCol + t * 128,
@@ -392,6 +393,7 @@ __global__ void __launch_bounds__(TcCfg::kThreads, 1)
               umma_commit(&pv_done[t]);
             }
           }
+          if (!ok) break;
           umma_commit(&slot_empty[pos_v(j) % NS]);
         }
       }
@@ -426,9 +428,6 @@ __global__ void __launch_bounds__(TcCfg::kThreads, 1)
       ok = __all_sync(0xffffffffu, mbar_wait_fast(&s_full[t], j & 1, abort_flag));
       if (!ok) break;
       tc_fence_after();
-      // s_free and p_full complete once per block with 256 arrivals: a tile whose partner has no
-      // block j (tile A's blocks end first; tile B may have none) arrives for both.
-      const uint32_t arrive_cnt = j < nblk_t[1 - t] ? 1u : 2u;
       const int k0 = key_lo + j * TcCfg::kBlockKeys;
       const bool need_mask =
           (k0 + TcCfg::kBlockKeys - 1 > qpos) || (k0 + TcCfg::kBlockKeys > key_end);
@@ -485,7 +484,7 @@ __global__ void __launch_bounds__(TcCfg::kThreads, 1)
         tmem_ld32(s_addr + 96, s3);
         tmem_wait_ld();
         tc_fence_before();
-        mbar_arrive_cnt(s_free, arrive_cnt);  // the MMA may now overwrite S_t with S_t(j + 1)
+        mbar_arrive(&s_free[t]);  // the MMA may now overwrite S_t with S_t(j + 1)
         const float neg_mu = m == ninf ? 0.f : -m;
         const float2 nm2 = make_float2(neg_mu, neg_mu);
         if (warp_masks) {
@@ -534,7 +533,7 @@ __global__ void __launch_bounds__(TcCfg::kThreads, 1)
       }
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive_cnt(p_full, arrive_cnt);
+      mbar_arrive(&p_full[t]);
     }
     if (!ok) {
       if (lane == 0) {

@@ -1,4 +1,5 @@
-"""CUDA-graph capture of a whole decode step (28 layers of kernel A + attention).
+"""CUDA-graph capture of whole steps (every layer's kernel A + attention): decode, chunked
+prefill on the tensor-core kernel, and a shared-prefix (cascade) group.
 
 The C-ABI calls neither allocate nor synchronise, so once the first (eager) call on a device has
 set kernel attributes, built the pool's tensor maps and allocated the step's workspace, the step
@@ -14,15 +15,22 @@ import torch
 from miniserve_b200.attention import attend, build_attention_metadata
 from miniserve_b200.kv_pool import allocate_kv_cache
 from miniserve_b200.qwen3_attention import qk_norm_rope_scatter
-from miniserve_b200.workloads import config2, rope_tables
+from miniserve_b200.workloads import config2, config3, config4, rope_tables
 
 pytestmark = pytest.mark.gpu
 
 
-def test_graph_replay_matches_eager(cuda_device: torch.device) -> None:
+@pytest.mark.parametrize("workload", ["config2_32rows", "config3", "config4_64rows"])
+def test_graph_replay_matches_eager(workload: str, cuda_device: torch.device) -> None:
+    """Decode rows with forced splits (kernels A, B, C), config 3's chunks (kernel D beside the
+    decode kernel) and a cascade group (kernel D's prefix partials merged by kernel B)."""
     dev = cuda_device
-    layers = 28
-    batch = config2(seed=5, num_seqs=32)
+    if workload == "config2_32rows":
+        layers, batch, split = 28, config2(seed=5, num_seqs=32), 16
+    elif workload == "config3":
+        layers, batch, split = 4, config3(seed=5), 0
+    else:
+        layers, batch, split = 4, config4(seed=5, num_seqs=64), 0
     t = batch.num_tokens
     g = torch.Generator(device=dev).manual_seed(5)
     pool, views = allocate_kv_cache(layers, batch.num_blocks, 8, dev, zero=False)
@@ -35,8 +43,13 @@ def test_graph_replay_matches_eager(cuda_device: torch.device) -> None:
     pos = torch.from_numpy(batch.positions).to(dev)
     slots = torch.from_numpy(batch.slots).to(dev)
     cos, sin = cos_t[pos], sin_t[pos]
-    meta = build_attention_metadata(batch.chunks, slots, 16, pages_per_split=16)
-    assert meta.info.n_combine > 0
+    meta = build_attention_metadata(batch.chunks, slots, 16, pages_per_split=split)
+    if workload == "config2_32rows":
+        assert meta.info.n_combine > 0
+    elif workload == "config3":
+        assert meta.info.n_tc_items > 0
+    else:
+        assert meta.info.n_cascade == 1
     q_buf = torch.empty(t, 16, 128, dtype=torch.bfloat16, device=dev)
     out = torch.empty(layers, t, 16, 128, dtype=torch.bfloat16, device=dev)
 
