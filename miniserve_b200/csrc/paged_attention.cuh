@@ -102,14 +102,29 @@ __device__ __forceinline__ void attend_page(uint32_t stage, const uint32_t (&qf)
   mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
   mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
   mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-  const float mn0 = fmaxf(m[0], mx0);
-  const float mn1 = fmaxf(m[1], mx1);
-  const float mu0 = mn0 == ninf ? 0.f : mn0;
-  const float mu1 = mn1 == ninf ? 0.f : mn1;
-  const float al0 = fast_exp2(m[0] - mu0);
-  const float al1 = fast_exp2(m[1] - mu1);
-  m[0] = mn0;
-  m[1] = mn1;
+  // The running max only moves (and O is rescaled) when a row's page max exceeds it by more
+  // than 2^8, so p stays below 2^8 and most pages skip the 64 multiplies of the rescale.
+  float al0 = 1.f, al1 = 1.f;
+  const bool up0 = mx0 > m[0] + 8.f, up1 = mx1 > m[1] + 8.f;
+  if (__any_sync(0xffffffffu, up0 || up1)) {
+    if (up0) {
+      al0 = fast_exp2(m[0] - mx0);
+      m[0] = mx0;
+    }
+    if (up1) {
+      al1 = fast_exp2(m[1] - mx1);
+      m[1] = mx1;
+    }
+#pragma unroll
+    for (int n = 0; n < 16; ++n) {
+      o[n][0] *= al0;
+      o[n][1] *= al0;
+      o[n][2] *= al1;
+      o[n][3] *= al1;
+    }
+  }
+  const float mu0 = m[0] == ninf ? 0.f : m[0];
+  const float mu1 = m[1] == ninf ? 0.f : m[1];
   float p0[4], p1[4];
   p0[0] = fast_exp2(s0[0] - mu0);
   p0[1] = fast_exp2(s0[1] - mu0);
@@ -121,13 +136,6 @@ __device__ __forceinline__ void attend_page(uint32_t stage, const uint32_t (&qf)
   p1[3] = fast_exp2(s1[3] - mu1);
   l[0] = l[0] * al0 + ((p0[0] + p0[1]) + (p1[0] + p1[1]));
   l[1] = l[1] * al1 + ((p0[2] + p0[3]) + (p1[2] + p1[3]));
-#pragma unroll
-  for (int n = 0; n < 16; ++n) {
-    o[n][0] *= al0;
-    o[n][1] *= al0;
-    o[n][2] *= al1;
-    o[n][3] *= al1;
-  }
   const uint32_t pa[4] = {pack_bf16(p0[0], p0[1]), pack_bf16(p0[2], p0[3]),
                           pack_bf16(p1[0], p1[1]), pack_bf16(p1[2], p1[3])};
   {
