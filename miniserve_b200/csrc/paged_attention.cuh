@@ -79,11 +79,8 @@ __device__ __forceinline__ void attend_page(uint32_t stage, const uint32_t (&qf)
     }
   }
   const float ninf = -INFINITY;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    s0[i] *= scale_log2;
-    s1[i] *= scale_log2;
-  }
+  // Scores stay unscaled (scale_log2 > 0 commutes with max); the scale is folded into the
+  // exponent's FMA below.
   if (need_mask) {
     const int ka = key0 + 2 * (lane & 3);
     const int kb = ka + 8;
@@ -102,6 +99,8 @@ __device__ __forceinline__ void attend_page(uint32_t stage, const uint32_t (&qf)
   mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
   mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
   mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+  mx0 *= scale_log2;
+  mx1 *= scale_log2;
   // The running max only moves (and O is rescaled) when a row's page max exceeds it by more
   // than 2^8, so p stays below 2^8 and most pages skip the 64 multiplies of the rescale.
   float al0 = 1.f, al1 = 1.f;
@@ -126,14 +125,14 @@ __device__ __forceinline__ void attend_page(uint32_t stage, const uint32_t (&qf)
   const float mu0 = m[0] == ninf ? 0.f : m[0];
   const float mu1 = m[1] == ninf ? 0.f : m[1];
   float p0[4], p1[4];
-  p0[0] = fast_exp2(s0[0] - mu0);
-  p0[1] = fast_exp2(s0[1] - mu0);
-  p0[2] = fast_exp2(s0[2] - mu1);
-  p0[3] = fast_exp2(s0[3] - mu1);
-  p1[0] = fast_exp2(s1[0] - mu0);
-  p1[1] = fast_exp2(s1[1] - mu0);
-  p1[2] = fast_exp2(s1[2] - mu1);
-  p1[3] = fast_exp2(s1[3] - mu1);
+  p0[0] = fast_exp2(__fmaf_rn(s0[0], scale_log2, -mu0));
+  p0[1] = fast_exp2(__fmaf_rn(s0[1], scale_log2, -mu0));
+  p0[2] = fast_exp2(__fmaf_rn(s0[2], scale_log2, -mu1));
+  p0[3] = fast_exp2(__fmaf_rn(s0[3], scale_log2, -mu1));
+  p1[0] = fast_exp2(__fmaf_rn(s1[0], scale_log2, -mu0));
+  p1[1] = fast_exp2(__fmaf_rn(s1[1], scale_log2, -mu0));
+  p1[2] = fast_exp2(__fmaf_rn(s1[2], scale_log2, -mu1));
+  p1[3] = fast_exp2(__fmaf_rn(s1[3], scale_log2, -mu1));
   l[0] = l[0] * al0 + ((p0[0] + p0[1]) + (p1[0] + p1[1]));
   l[1] = l[1] * al1 + ((p0[2] + p0[3]) + (p1[2] + p1[3]));
   const uint32_t pa[4] = {pack_bf16(p0[0], p0[1]), pack_bf16(p0[2], p0[3]),
