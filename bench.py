@@ -260,6 +260,37 @@ def run_ours(args: argparse.Namespace, rank: int, world: int, device: torch.devi
     if status:
         raise RuntimeError(f"device status {status:#x} after timing")
 
+    # ---- config 3's two parts, timed apart (decode rows; prefill chunks) ----
+    parts = None
+    dec_chunks = [c for c in batch.chunks if c.num_new <= 64]
+    pre_chunks = [c for c in batch.chunks if c.num_new > 64]
+    if dec_chunks and pre_chunks:
+        parts = {}
+        k_cache, v_cache = views[0]
+        for name, sub in (("decode_rows", dec_chunks), ("prefill_chunks", pre_chunks)):
+            sub_meta = build_attention_metadata(sub, slot_mapping, 16,
+                                                pages_per_split=args.pages_per_split)
+            attend(q_buf, k_cache, v_cache, sub_meta, scale, out=out_all[0])
+            torch.cuda.synchronize(device)
+            g_sub = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g_sub):
+                for _ in range(10):
+                    attend(q_buf, k_cache, v_cache, sub_meta, scale, out=out_all[0])
+            g_sub.replay()
+            torch.cuda.synchronize(device)
+            p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            p0.record(stream)
+            g_sub.replay()
+            p1.record(stream)
+            torch.cuda.synchronize(device)
+            us = p0.elapsed_time(p1) * 1e3 / 10
+            del g_sub
+            sub_batch = type(batch)(batch.name, sub, batch.num_blocks)
+            sub_bytes, _, sub_flops = attention_bytes(sub_batch)
+            parts[name] = {"us_per_layer": us, "GB/s": sub_bytes / (us * 1e-6) / 1e9,
+                           "TFLOPS_causal": sub_flops / (us * 1e-6) / 1e12,
+                           "timing": "CUDA-graph replay of 10 calls, this part alone"}
+
     # ---- e2e: through the public API with host buffers ----
     qkv_host = qkv_all.cpu().pin_memory()
     out_host = torch.empty(LAYERS, t, H, D, dtype=torch.bfloat16).pin_memory()
@@ -371,6 +402,7 @@ def run_ours(args: argparse.Namespace, rank: int, world: int, device: torch.devi
         "launches_per_step": LAYERS * launches_per_layer,
         "h2d": h2d,
         "d2h": d2h,
+        "parts": parts,
         "plan": {"decode_items": info.n_decode_items, "tile_items": info.n_tile_items,
                  "tc_items": info.n_tc_items, "combine": info.n_combine,
                  "pages_per_split": info.pages_per_split},
@@ -572,6 +604,8 @@ def main() -> None:
             "clocks": r["clocks"],
             "plan": r["plan"],
         }
+        if r["parts"] is not None:
+            line["parts"] = r["parts"]
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.barrier()

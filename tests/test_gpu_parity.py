@@ -119,6 +119,22 @@ def test_tensor_core_prefill_edges(rows, cuda_device: torch.device) -> None:
         assert err <= ATOL, (split, err)
 
 
+def test_config5_contexts_on_a_non_aliased_subset(cuda_device: torch.device) -> None:
+    """Config 5's heavy-tailed contexts (logU[512, 32768]): its shortest, longest and quantile
+    rows, each with its own blocks (no pool aliasing), against the fp32 oracle; automatic and
+    forced splits."""
+    import numpy as np
+
+    from miniserve_b200.workloads import config5_contexts
+
+    ctx = np.sort(config5_contexts(seed=0))
+    pick = [ctx[0], ctx[-1]] + [ctx[int(q * (len(ctx) - 1))] for q in (0.1, 0.5, 0.9, 0.99)]
+    rows = [(1, int(L) - 1) for L in pick] + [(5, int(pick[1]) - 5)]  # and one verify row
+    for split in (0, 64):
+        err = _random_case_vs_fp32(custom(rows, seed=21), 21, split, cuda_device)
+        assert err <= ATOL, (split, err)
+
+
 @pytest.mark.parametrize("num_seqs", [16, 64, 512], ids=["16_rows", "64_rows", "config4"])
 def test_cascade_shared_prefix(num_seqs: int, cuda_device: torch.device) -> None:
     """Config 4's geometry (5-token verify rows sharing a 1024-token prefix, 64..256 own tokens):
