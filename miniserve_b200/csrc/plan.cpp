@@ -39,8 +39,15 @@ constexpr int kRec = 8;
 constexpr int kDecodeMaxTokens = 8;  // backends.py:32 SHORT_QUERY: the batched (short) path
 constexpr int kTileTokens = 64;      // longest chunk of the mma.sync tile kernel (128 rows)
 constexpr int kTcTokens = 128;       // query tokens per tensor-core work item (2 x 128 rows)
-constexpr int kItemsPerSm = 1;       // automatic split: about one item per SM per KV head
-constexpr int kMinSplitPages = 32;   // a split streams at least 256 KiB per KV head
+// Automatic split of decode / small-tile items: the smallest split (a multiple of 8 pages, at
+// least kMinSplitPages) whose items fit one resident wave of CTAs -- kDecodeCtasPerSm per SM,
+// kTcAssumedKvHeads CTAs per item -- or no split (up to kMaxSplitPages) when the rows alone
+// exceed a wave.  Measured on 1x B200 (us per attention call): 1 row of 32K tokens 36.4 with
+// 64-page splits vs 50.2 with 32; 4 x 16K 47.6 (128) vs 64.5 (32); config 3's 48 decode rows
+// 41.0 unsplit vs 46.5 (32).  Splits that leave a thin second wave are the worst case.
+constexpr int kDecodeCtasPerSm = 2;
+constexpr int kMinSplitPages = 64;
+constexpr int kMaxSplitPages = 512;
 constexpr int kTcBlockPages = 8;     // 128-key blocks of the tensor-core kernel
 constexpr int kTcMinSplitPages = 32; // forced splits: tensor-core items cover at least 4 blocks
 // Automatic tensor-core plan.  The planner does not see the head count; it sizes work for
@@ -118,7 +125,6 @@ extern "C" int ms_plan_build(int32_t num_seqs, const int32_t* flat_start, const 
   std::vector<Item> tiles;
   tiles.reserve(num_seqs);
   int64_t total_pages = 0;
-  int64_t short_pages = 0;  // pages of tiles that run on the decode / small-tile kernels
   for (int i = 0; i < num_seqs; ++i) {
     const int64_t n = num_new[i], c = num_cached[i], f = flat_start[i];
     const int64_t tlen = table_offsets[i + 1] - table_offsets[i];
@@ -144,7 +150,6 @@ extern "C" int ms_plan_build(int32_t num_seqs, const int32_t* flat_start, const 
       const int pages = static_cast<int>((c + t0 + nq + block_size - 1) / block_size);
       tiles.push_back({i, static_cast<int>(t0), nq, 0, pages, -1});
       total_pages += pages;
-      if (n <= kTileTokens) short_pages += pages;
     }
   }
 
@@ -187,7 +192,6 @@ extern "C" int ms_plan_build(int32_t num_seqs, const int32_t* flat_start, const 
         groups.push_back({i, j, static_cast<int>(shared), static_cast<int>(tokens)});
         for (int k = i; k < j; ++k) {
           cascade_pages[k] = static_cast<int>(shared);
-          short_pages -= shared;
         }
         i = j;
       } else {
@@ -196,13 +200,29 @@ extern "C" int ms_plan_build(int32_t num_seqs, const int32_t* flat_start, const 
     }
   }
 
-  // Split size for the bandwidth-bound kernels: enough items to fill the GPU several times
-  // over, but never so short that a CTA's start-up latency dominates its streaming.
+  // Split size for the bandwidth-bound kernels (see kDecodeCtasPerSm).
   int split = pages_per_split;
   if (split == 0) {
-    const int64_t target = static_cast<int64_t>(num_sms) * kItemsPerSm;
-    split = static_cast<int>(std::clamp<int64_t>((short_pages + target - 1) / std::max<int64_t>(target, 1),
-                                                 kMinSplitPages, 512));
+    const int64_t target_items =
+        std::max<int64_t>(1, static_cast<int64_t>(num_sms) * kDecodeCtasPerSm / kTcAssumedKvHeads);
+    auto items_at = [&](int p) {
+      int64_t items = 0;
+      for (const Item& t : tiles)
+        if (num_new[t.seq] <= kTileTokens && cascade_pages[t.seq] == 0) items += (t.pe + p - 1) / p;
+      return items;
+    };
+    // items_at() does not grow with the split, so the smallest fitting split is found by
+    // bisection over multiples of 8 pages.
+    int lo = kMinSplitPages / 8, hi = kMaxSplitPages / 8;
+    if (items_at(hi * 8) > target_items) {
+      split = kMaxSplitPages;
+    } else {
+      while (lo < hi) {
+        const int mid = (lo + hi) / 2;
+        if (items_at(mid * 8) <= target_items) hi = mid; else lo = mid + 1;
+      }
+      split = lo * 8;
+    }
   }
 
   std::vector<Item> dec, til, tcv, comb;
