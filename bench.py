@@ -59,6 +59,9 @@ def parse() -> argparse.Namespace:
                    help="cfg2 is the headline; cfg1 (8 short decode rows), cfg3 (mixed prefill), "
                         "cfg4 (prefix + verify) and cfg5 (box scale: 8192 rows sharded over the "
                         "ranks) are reported alongside")
+    p.add_argument("--no-qkv-part", action="store_true",
+                   help="skip timing kernel E (qkv projection + norm/RoPE/scatter) beside "
+                        "cuBLAS + kernel A")
     p.add_argument("--pool-gb", type=float, default=150.0,
                    help="cfg5: per-GPU pool shared by all layers")
     return p.parse_args()
@@ -148,6 +151,70 @@ def attention_bytes(batch) -> tuple[int, int, int]:
     kern_a = t * (H + 2 * KVH) * D * 2 + t * H * D * 2 + t * 2 * KVH * D * 2 + t * D * 4 * 2 + t * 8
     pairs = sum(c.num_new * c.num_cached + c.num_new * (c.num_new + 1) // 2 for c in batch.chunks)
     return attn, kern_a, 4 * D * H * pairs
+
+
+def time_qkv_projection(t: int, views, qw, kw, cos, sin, slot_mapping, layers: int,
+                        device: torch.device, stream) -> dict:
+    """Kernel E (the qkv projection with kernel A as its epilogue, qwen3.py:94-98 +
+    backends.py:159-160) beside what it replaces, cuBLAS + kernel A, on this workload's tokens.
+    Each layer has its own x [T, 1024] and W [4096, 1024] (28 x 8 MiB of weights > L2); both
+    forms are captured as one CUDA graph over the layers and replayed."""
+    from miniserve_b200.qwen3_attention import qk_norm_rope_scatter, qkv_proj_norm_rope_scatter
+
+    hidden, width = 1024, (H + 2 * KVH) * D
+    g = torch.Generator(device=device).manual_seed(4321)
+    x = torch.randn(layers, t, hidden, generator=g, device=device, dtype=torch.bfloat16)
+    w = (torch.randn(layers, width, hidden, generator=g, device=device) / 32).bfloat16()
+    qkv = torch.empty(t, width, dtype=torch.bfloat16, device=device)
+    q_buf = torch.empty(t, H, D, dtype=torch.bfloat16, device=device)
+
+    def fused() -> None:
+        for layer in range(layers):
+            qkv_proj_norm_rope_scatter(x[layer], w[layer], qw[layer], kw[layer], 1e-6, cos, sin,
+                                       slot_mapping, *views[layer], H, q_out=q_buf)
+
+    def unfused() -> None:
+        for layer in range(layers):
+            torch.matmul(x[layer], w[layer].t(), out=qkv)
+            qk_norm_rope_scatter(qkv, qw[layer], kw[layer], 1e-6, cos, sin, slot_mapping,
+                                 *views[layer], H, q_out=q_buf)
+
+    res = {}
+    for name, fn in (("fused_kernel_e", fused), ("cublas_plus_kernel_a", unfused)):
+        fn()
+        torch.cuda.synchronize(device)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            fn()
+        graph.replay()
+        torch.cuda.synchronize(device)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(5):
+            graph.replay()
+        e1.record(stream)
+        torch.cuda.synchronize(device)
+        res[name] = e0.elapsed_time(e1) * 1e3 / (5 * layers)
+        del graph
+    pk, src = peaks()
+    flops = 2.0 * t * hidden * width
+    # W and x read once, q and the K/V rows written once (the projection output is not stored).
+    nbytes = 2.0 * (width * hidden + t * hidden + t * width)
+    us = res["fused_kernel_e"]
+    floor_us = max(flops / (float(pk["bf16_tflops"]) * 1e12),
+                   nbytes / (float(pk["hbm_gbs"]) * 1e9)) * 1e6
+    return {
+        "tokens": t,
+        "hidden": hidden,
+        "us_per_layer": {k: round(v, 2) for k, v in res.items()},
+        "speedup_vs_cublas_plus_a": res["cublas_plus_kernel_a"] / us,
+        "fused_TFLOPS": flops / (us * 1e-6) / 1e12,
+        "fused_GBps_algorithmic": nbytes / (us * 1e-6) / 1e9,
+        "roofline_floor_us": floor_us,
+        "frac_of_roofline": floor_us / us,
+        "peak_source": src,
+        "timing": f"CUDA-graph replay of {layers} layers x 5, per layer; distinct W per layer",
+    }
 
 
 def run_ours(args: argparse.Namespace, rank: int, world: int, device: torch.device) -> dict:
@@ -291,6 +358,14 @@ def run_ours(args: argparse.Namespace, rank: int, world: int, device: torch.devi
                            "TFLOPS_causal": sub_flops / (us * 1e-6) / 1e12,
                            "timing": "CUDA-graph replay of 10 calls, this part alone"}
 
+    qkv_part = None
+    if not args.no_qkv_part and rank == 0:
+        qkv_part = time_qkv_projection(t, views, qw, kw, cos, sin, slot_mapping, LAYERS, device,
+                                       stream)
+        status = _capi.device_status(int(stream.cuda_stream))
+        if status:
+            raise RuntimeError(f"device status {status:#x} after the qkv projection timing")
+
     # ---- e2e: through the public API with host buffers ----
     qkv_host = qkv_all.cpu().pin_memory()
     out_host = torch.empty(LAYERS, t, H, D, dtype=torch.bfloat16).pin_memory()
@@ -403,6 +478,7 @@ def run_ours(args: argparse.Namespace, rank: int, world: int, device: torch.devi
         "h2d": h2d,
         "d2h": d2h,
         "parts": parts,
+        "qkv_projection": qkv_part,
         "plan": {"decode_items": info.n_decode_items, "tile_items": info.n_tile_items,
                  "tc_items": info.n_tc_items, "combine": info.n_combine,
                  "pages_per_split": info.pages_per_split},
@@ -606,6 +682,8 @@ def main() -> None:
         }
         if r["parts"] is not None:
             line["parts"] = r["parts"]
+        if r["qkv_projection"] is not None:
+            line["qkv_projection"] = r["qkv_projection"]
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.barrier()

@@ -130,6 +130,26 @@ MS_API int ms_qk_norm_rope_scatter(const void* qkv, int64_t qkv_row_stride, int3
                             int64_t q_out_row_stride, void* k_cache, void* v_cache,
                             int32_t num_blocks, void* stream);
 
+/* ---- Kernel E: qkv projection with kernel A as its epilogue -----------------------------------
+ * Replaces, for one layer, `self.qkv_proj(x)` and the split/q_norm/k_norm/apply_rope after it
+ * (qwen3.py:94-98, the projection built at qwen3.py:75-77 as nn.Linear(hidden, (H+2*KVH)*128,
+ * bias=False)) plus the K/V index_copy_ at backends.py:159-160, in one tensor-core launch: the
+ * projection output never reaches memory.  x is [T, hidden] bf16 (hidden a multiple of 64), w_qkv
+ * the projection weight [(H+2*KVH)*128, hidden] bf16 as nn.Linear stores it; every other argument
+ * means what it means for ms_qk_norm_rope_scatter, with x, w_qkv, q_out and the two norm weights
+ * 16-byte aligned (row strides multiples of 8 elements).  The result equals
+ * ms_qk_norm_rope_scatter applied to bf16(x @ w_qkv^T) except where the GEMM's fp32 accumulation
+ * order moves a projection output by one bf16 ulp. */
+MS_API int ms_qkv_proj_norm_rope_scatter(const void* x, int64_t x_row_stride, int32_t num_tokens,
+                                  int32_t hidden, const void* w_qkv, int64_t w_row_stride,
+                                  int32_t num_heads, int32_t num_kv_heads, const void* q_weight,
+                                  const void* k_weight, float eps, const float* cos,
+                                  const float* sin, int64_t cs_row_stride,
+                                  const int64_t* positions, int64_t max_positions,
+                                  const int64_t* slot_mapping, void* q_out,
+                                  int64_t q_out_row_stride, void* k_cache, void* v_cache,
+                                  int32_t num_blocks, void* stream);
+
 /* Scatter only (backends.py:159-160): k, v [T, KVH, 128] with the given row strides. */
 MS_API int ms_kv_scatter(const void* k, int64_t k_row_stride, const void* v, int64_t v_row_stride,
                   int32_t num_tokens, int32_t num_kv_heads, const int64_t* slot_mapping,

@@ -34,6 +34,7 @@ EXPORTED = (
     "ms_plan_build",
     "ms_prepare_step",
     "ms_qk_norm_rope_scatter",
+    "ms_qkv_proj_norm_rope_scatter",
     "ms_kv_scatter",
     "ms_paged_attention",
     "ms_paged_attention_noalloc",
@@ -82,6 +83,11 @@ _SIGNATURES = {
         C.c_int,
         [_P, _I64, _I32, _I32, _I32, _P, _P, C.c_float, _P, _P, _I64, _P, _I64, _P, _P, _I64,
          _P, _P, _I32, _P],
+    ),
+    "ms_qkv_proj_norm_rope_scatter": (
+        C.c_int,
+        [_P, _I64, _I32, _I32, _P, _I64, _I32, _I32, _P, _P, C.c_float, _P, _P, _I64, _P, _I64,
+         _P, _P, _I64, _P, _P, _I32, _P],
     ),
     "ms_kv_scatter": (C.c_int, [_P, _I64, _P, _I64, _I32, _I32, _P, _P, _P, _I32, _P]),
     "ms_paged_attention": (

@@ -16,6 +16,7 @@
 #include "norm_rope_scatter.cuh"
 #include "paged_attention.cuh"
 #include "prefill_tc.cuh"
+#include "qkv_proj_tc.cuh"
 
 namespace ms_host {
 
@@ -109,6 +110,32 @@ static int kv_tensor_map(const void* k_cache, int num_blocks, int num_kv, int bo
   return MS_OK;
 }
 
+// A row-major bf16 matrix [rows, cols] (row stride in elements) as a 2-D tensor map with
+// 128-byte-swizzled {64 columns, 128 rows} boxes: one K-major tcgen05 operand tile.  Rows past
+// the end read as zeros.
+static int matrix_tile_map(const void* base, int64_t rows, int64_t cols, int64_t row_stride,
+                           CUtensorMap* out) {
+  auto fn = encode_fn();
+  if (fn == nullptr) {
+    set_error("cuTensorMapEncodeTiled is unavailable from the driver");
+    return MS_ERR_CUDA;
+  }
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_stride) * 2};
+  const cuuint32_t box[2] = {64, 128};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims,
+                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled (matrix) failed with CUresult " +
+              std::to_string(static_cast<int>(r)));
+    return MS_ERR_CUDA;
+  }
+  return MS_OK;
+}
+
 // ---- attention launch configurations --------------------------------------------------------
 
 constexpr int kDecodeWarps = 4, kDecodeStages = 8;
@@ -136,7 +163,30 @@ static int ensure_smem_attrs() {
   e = cudaFuncSetAttribute(ms::prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            ms::TcCfg::kSmemBytes);
   if (e != cudaSuccess) return cuda_fail("cudaFuncSetAttribute(tc)", e);
+  e = cudaFuncSetAttribute(ms::qkv_proj_norm_rope_kernel<1>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, ms::QkvCfg<1>::kSmemBytes);
+  if (e != cudaSuccess) return cuda_fail("cudaFuncSetAttribute(qkv 1)", e);
+  e = cudaFuncSetAttribute(ms::qkv_proj_norm_rope_kernel<2>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, ms::QkvCfg<2>::kSmemBytes);
+  if (e != cudaSuccess) return cuda_fail("cudaFuncSetAttribute(qkv 2)", e);
   done[dev] = true;
+  return MS_OK;
+}
+
+static int sm_count(int* out) {
+  // Per device, cached.
+  static std::mutex mu;
+  static int counts[64] = {0};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail("cudaGetDevice", e);
+  if (dev < 0 || dev >= 64) return MS_ERR_ARG;
+  std::lock_guard<std::mutex> lock(mu);
+  if (counts[dev] == 0) {
+    e = cudaDeviceGetAttribute(&counts[dev], cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return cuda_fail("cudaDeviceGetAttribute(SM count)", e);
+  }
+  *out = counts[dev];
   return MS_OK;
 }
 
@@ -281,6 +331,97 @@ extern "C" int ms_qk_norm_rope_scatter(const void* qkv, int64_t qkv_row_stride, 
       <<<static_cast<unsigned>(blocks), kWarps * 32, 0, static_cast<cudaStream_t>(stream)>>>(a, st);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail("qk_norm_rope_scatter launch", e);
+  return MS_OK;
+}
+
+extern "C" int ms_qkv_proj_norm_rope_scatter(
+    const void* x, int64_t x_row_stride, int32_t num_tokens, int32_t hidden, const void* w_qkv,
+    int64_t w_row_stride, int32_t num_heads, int32_t num_kv_heads, const void* q_weight,
+    const void* k_weight, float eps, const float* cos, const float* sin, int64_t cs_row_stride,
+    const int64_t* positions, int64_t max_positions, const int64_t* slot_mapping, void* q_out,
+    int64_t q_out_row_stride, void* k_cache, void* v_cache, int32_t num_blocks, void* stream) {
+  if (num_tokens < 0 || num_heads <= 0 || num_kv_heads <= 0 || hidden <= 0 || hidden % 64) {
+    set_error("ms_qkv_proj_norm_rope_scatter: need num_tokens >= 0, heads > 0 and hidden a "
+              "positive multiple of 64");
+    return MS_ERR_ARG;
+  }
+  if (num_tokens == 0) return MS_OK;
+  int rc = check_pool(k_cache, v_cache, num_blocks, num_kv_heads);
+  if (rc) return rc;
+  if (!x || !w_qkv || !q_weight || !k_weight || !cos || !sin || !slot_mapping || !q_out) {
+    set_error("ms_qkv_proj_norm_rope_scatter: null pointer argument");
+    return MS_ERR_ARG;
+  }
+  if (x_row_stride < hidden || w_row_stride < hidden || x_row_stride % 8 || w_row_stride % 8 ||
+      q_out_row_stride < static_cast<int64_t>(num_heads) * ms::kHeadDim || q_out_row_stride % 8 ||
+      cs_row_stride < ms::kHeadDim || cs_row_stride % 4 || !aligned(x, 16) || !aligned(w_qkv, 16) ||
+      !aligned(q_weight, 16) || !aligned(k_weight, 16) || !aligned(q_out, 16) ||
+      !aligned(cos, 16) || !aligned(sin, 16)) {
+    set_error("ms_qkv_proj_norm_rope_scatter: strides/alignment (x, w_qkv, q_out rows and the "
+              "norm weights 16-byte aligned; cos/sin rows 16-byte aligned)");
+    return MS_ERR_ARG;
+  }
+  if (positions != nullptr && max_positions <= 0) {
+    set_error("ms_qkv_proj_norm_rope_scatter: positions given with an empty table");
+    return MS_ERR_ARG;
+  }
+  const int64_t m_tiles = (static_cast<int64_t>(num_tokens) + 127) / 128;
+  if (m_tiles > 65535) {
+    set_error("ms_qkv_proj_norm_rope_scatter: batch too large");
+    return MS_ERR_ARG;
+  }
+  rc = ensure_smem_attrs();
+  if (rc) return rc;
+  unsigned* st = status_ptr(&rc);
+  if (rc) return rc;
+  const int rows = num_heads + 2 * num_kv_heads;
+  CUtensorMap xmap, wmap;
+  rc = matrix_tile_map(x, num_tokens, hidden, x_row_stride, &xmap);
+  if (rc) return rc;
+  rc = matrix_tile_map(w_qkv, static_cast<int64_t>(rows) * ms::kHeadDim, hidden, w_row_stride,
+                       &wmap);
+  if (rc) return rc;
+  ms::QkvArgs qa;
+  ms::NormRopeArgs& a = qa.e;
+  a.qkv = nullptr;
+  a.qkv_row_stride = 0;
+  a.q_weight = static_cast<const __nv_bfloat16*>(q_weight);
+  a.k_weight = static_cast<const __nv_bfloat16*>(k_weight);
+  a.eps = eps;
+  a.cos = cos;
+  a.sin = sin;
+  a.cs_row_stride = cs_row_stride;
+  a.positions = reinterpret_cast<const long long*>(positions);
+  a.max_positions = max_positions;
+  a.slots = reinterpret_cast<const long long*>(slot_mapping);
+  a.q_out = static_cast<__nv_bfloat16*>(q_out);
+  a.q_out_row_stride = q_out_row_stride;
+  a.k_pool = static_cast<__nv_bfloat16*>(k_cache);
+  a.head_stride = ms::kPageKVBytes / 2;
+  a.block_stride = static_cast<long long>(num_kv_heads) * a.head_stride;
+  a.num_slots = static_cast<long long>(num_blocks) * ms::kBlockTokens;
+  a.num_tokens = num_tokens;
+  a.num_heads = num_heads;
+  a.num_kv = num_kv_heads;
+  qa.hidden = hidden;
+  int sms = 0;
+  rc = sm_count(&sms);
+  if (rc) return rc;
+  // Two heads per tile (less L2 traffic per flop) once that still gives every SM two tiles and
+  // the heads pair up by kind; one head per tile otherwise (more tiles for small batches).
+  const bool pairs = num_heads % 2 == 0 && num_kv_heads % 2 == 0 &&
+                     m_tiles * (rows / 2) >= 2 * static_cast<int64_t>(sms);
+  qa.num_tiles = static_cast<int>(m_tiles * (pairs ? rows / 2 : rows));
+  const int grid = qa.num_tiles < sms ? qa.num_tiles : sms;  // persistent: one CTA per SM
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (pairs)
+    ms::qkv_proj_norm_rope_kernel<2>
+        <<<grid, ms::QkvCfg<2>::kThreads, ms::QkvCfg<2>::kSmemBytes, s>>>(xmap, wmap, qa, st);
+  else
+    ms::qkv_proj_norm_rope_kernel<1>
+        <<<grid, ms::QkvCfg<1>::kThreads, ms::QkvCfg<1>::kSmemBytes, s>>>(xmap, wmap, qa, st);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail("qkv_proj_norm_rope launch", e);
   return MS_OK;
 }
 

@@ -76,6 +76,60 @@ def qk_norm_rope_scatter(
     return q_out
 
 
+def qkv_proj_norm_rope_scatter(
+    x: Tensor,
+    w_qkv: Tensor,
+    q_weight: Tensor,
+    k_weight: Tensor,
+    eps: float,
+    cos: Tensor,
+    sin: Tensor,
+    slot_mapping: Tensor,
+    k_cache: Tensor,
+    v_cache: Tensor,
+    num_heads: int,
+    positions: Tensor | None = None,
+    q_out: Tensor | None = None,
+) -> Tensor:
+    """Kernel E: ``qkv_proj`` (``x @ w_qkv.T``, qwen3.py:94) with kernel A as its epilogue, in one
+    tensor-core launch.  Same outputs as ``qk_norm_rope_scatter(x @ w_qkv.T, ...)`` up to the
+    GEMM's fp32 accumulation order (a projection output may differ by one bf16 ulp)."""
+    nb, kvh = check_layer_views(k_cache, v_cache)
+    t = int(x.shape[0])
+    if x.dim() != 2 or x.stride(1) != 1 or x.dtype != torch.bfloat16:
+        raise ValueError("x must be bf16 [T, hidden] with unit column stride")
+    hidden = int(x.shape[1])
+    width = (num_heads + 2 * kvh) * HEAD_DIM
+    if (w_qkv.dim() != 2 or tuple(w_qkv.shape) != (width, hidden) or w_qkv.stride(1) != 1
+            or w_qkv.dtype != torch.bfloat16):
+        raise ValueError(f"w_qkv must be bf16 [{width}, {hidden}] with unit column stride")
+    if q_weight.dtype != torch.bfloat16 or k_weight.dtype != torch.bfloat16:
+        raise ValueError("q_norm / k_norm weights must be bf16")
+    if cos.dtype != torch.float32 or sin.dtype != torch.float32 or cos.stride(-1) != 1:
+        raise ValueError("cos/sin must be fp32 with unit column stride")
+    if sin.stride(0) != cos.stride(0):
+        raise ValueError("cos and sin must share a row stride")
+    if positions is None and cos.shape[0] < t:
+        raise ValueError("per-token cos/sin rows must cover every token")
+    if q_out is None:
+        q_out = torch.empty((t, num_heads, HEAD_DIM), dtype=torch.bfloat16, device=x.device)
+    pos_ptr, max_pos = None, 0
+    if positions is not None:
+        if positions.dtype != torch.int64:
+            raise ValueError("positions must be int64")
+        pos_ptr, max_pos = positions.data_ptr(), int(cos.shape[0])
+    lib = _capi.load()
+    rc = lib.ms_qkv_proj_norm_rope_scatter(
+        x.data_ptr(), int(x.stride(0)), t, hidden, w_qkv.data_ptr(), int(w_qkv.stride(0)),
+        num_heads, kvh, q_weight.data_ptr(), k_weight.data_ptr(), float(eps), cos.data_ptr(),
+        sin.data_ptr(), int(cos.stride(0)), pos_ptr, max_pos, slot_mapping.data_ptr(),
+        q_out.data_ptr(), _rows(q_out, "q_out"), k_cache.data_ptr(), v_cache.data_ptr(), nb,
+        _stream(x.device),
+    )
+    _capi.check(rc, "qkv_proj_norm_rope_scatter")
+    return q_out
+
+
 class Qwen3Attention(nn.Module):
     """Same constructor and forward as the reference module (qwen3.py:65-100)."""
 
