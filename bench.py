@@ -54,11 +54,14 @@ def parse() -> argparse.Namespace:
                    help="time eager launches instead of replaying the captured step")
     p.add_argument("--layers", type=int, default=LAYERS,
                    help="layers per step (28 for the headline; fewer only for small profiles)")
-    p.add_argument("--workload", choices=["cfg1", "cfg2", "cfg3", "cfg4", "cfg5"],
+    p.add_argument("--tokens", type=int, default=4096,
+                   help="--workload qkv: tokens per step")
+    p.add_argument("--workload", choices=["cfg1", "cfg2", "cfg3", "cfg4", "cfg5", "qkv"],
                    default="cfg2",
                    help="cfg2 is the headline; cfg1 (8 short decode rows), cfg3 (mixed prefill), "
                         "cfg4 (prefix + verify) and cfg5 (box scale: 8192 rows sharded over the "
-                        "ranks) are reported alongside")
+                        "ranks) are reported alongside; qkv times kernel E (qkv projection + "
+                        "norm/RoPE/scatter) beside cuBLAS + kernel A at --tokens tokens")
     p.add_argument("--no-qkv-part", action="store_true",
                    help="skip timing kernel E (qkv projection + norm/RoPE/scatter) beside "
                         "cuBLAS + kernel A")
@@ -215,6 +218,38 @@ def time_qkv_projection(t: int, views, qw, kw, cos, sin, slot_mapping, layers: i
         "peak_source": src,
         "timing": f"CUDA-graph replay of {layers} layers x 5, per layer; distinct W per layer",
     }
+
+
+def run_qkv_only(args: argparse.Namespace, rank: int, device: torch.device) -> None:
+    """--workload qkv: kernel E beside cuBLAS + kernel A on --tokens tokens (one sequence's
+    prefill positions, a permuted pool), --layers distinct layers per timed pass."""
+    from miniserve_b200 import _capi
+    from miniserve_b200.kv_pool import allocate_kv_cache
+    from miniserve_b200.workloads import rope_tables
+
+    if rank != 0:
+        return
+    t, layers = args.tokens, args.layers
+    nb = (t + 15) // 16 + 8
+    _pool, views = allocate_kv_cache(layers, nb, KVH, device)
+    g = torch.Generator(device=device).manual_seed(7)
+    qw = (1 + 0.1 * torch.randn(layers, D, generator=g, device=device)).bfloat16()
+    kw = (1 + 0.1 * torch.randn(layers, D, generator=g, device=device)).bfloat16()
+    cos_t, sin_t = rope_tables(D, t + 8, 1e6, device)
+    positions = torch.arange(t, device=device)
+    cos, sin = cos_t[positions], sin_t[positions]
+    slots = torch.randperm(nb * 16, generator=g, device=device)[:t]
+    stream = torch.cuda.current_stream(device)
+    r = time_qkv_projection(t, views, qw, kw, cos, sin, slots, layers, device, stream)
+    status = _capi.device_status(int(stream.cuda_stream))
+    if status:
+        raise RuntimeError(f"device status {status:#x}")
+    print(json.dumps({"metric": "qkv projection + q/k norm + RoPE + K/V scatter (us per layer)",
+                      "value": r["us_per_layer"]["fused_kernel_e"], "unit": "us",
+                      "higher_is_better": False, "n_gpus": 1, "dtype": "bf16",
+                      "data": "synthetic", "config": {"workload": f"qkv: {t} tokens, hidden "
+                                                      f"1024, 16q/8kv heads, {layers} layers"},
+                      "qkv_projection": r}), flush=True)
 
 
 def run_ours(args: argparse.Namespace, rank: int, world: int, device: torch.device) -> dict:
@@ -595,6 +630,13 @@ def main() -> None:
         build()
     if world > 1:
         torch.distributed.barrier()
+
+    if args.workload == "qkv":
+        run_qkv_only(args, rank, device)
+        if world > 1:
+            torch.distributed.barrier()
+            torch.distributed.destroy_process_group()
+        return
 
     r = run_ours(args, rank, world, device)
     ms = torch.tensor([r["total_ms"], r["e2e_ms"], r["attn_ms"], r["eager_ms"]],

@@ -126,26 +126,28 @@ __device__ __forceinline__ RowMeta ld_meta(uint32_t addr) {
   return m;
 }
 
+// A row's cos and sin at this lane's dims, rounded to bf16 pairs (kernel A: .to(bf16)).
+struct RopeRow {
+  uint32_t c01, c23, s01, s23;
+};
+
 // Kernel A's per-row work (lane = dims 4l..4l+3) for N staged rows of the tile's kHeads query or
-// key heads; the heads of a row share its cos/sin loads.
+// key heads, with the rows' cos/sin already in registers.
 template <int kHeads, int N>
 __device__ __forceinline__ void norm_rope_rows(const NormRopeArgs& a, uint32_t stage_base,
                                                uint32_t meta_base, int row0, int m0,
-                                               int head_row0, bool is_q, uint2 w2, int lane) {
+                                               int head_row0, bool is_q, uint2 w2,
+                                               const RopeRow* cs, int lane) {
   using Cfg = QkvCfg<kHeads>;
   const int d0 = lane * 4;
   uint2 raw[N][kHeads];
-  float4 c4[N], s4[N];
   long long slot[N];
 #pragma unroll
   for (int i = 0; i < N; ++i) {
-    const RowMeta m = ld_meta(meta_base + (row0 + i) * 16);
-    slot[i] = m.slot;
+    slot[i] = ld_meta(meta_base + (row0 + i) * 16).slot;
 #pragma unroll
     for (int h = 0; h < kHeads; ++h)
       raw[i][h] = ld_shared_v2(stage_base + (row0 + i) * Cfg::kRowPitch + h * 256 + lane * 8);
-    c4[i] = *reinterpret_cast<const float4*>(a.cos + m.cs_row * a.cs_row_stride + d0);
-    s4[i] = *reinterpret_cast<const float4*>(a.sin + m.cs_row * a.cs_row_stride + d0);
   }
   float ss[N][kHeads];
 #pragma unroll
@@ -169,10 +171,8 @@ __device__ __forceinline__ void norm_rope_rows(const NormRopeArgs& a, uint32_t s
   }
 #pragma unroll
   for (int i = 0; i < N; ++i) {
-    const __nv_bfloat162 c01 = as_bf2(pack_bf16(c4[i].x, c4[i].y));
-    const __nv_bfloat162 c23 = as_bf2(pack_bf16(c4[i].z, c4[i].w));
-    const __nv_bfloat162 s01 = as_bf2(pack_bf16(s4[i].x, s4[i].y));
-    const __nv_bfloat162 s23 = as_bf2(pack_bf16(s4[i].z, s4[i].w));
+    const __nv_bfloat162 c01 = as_bf2(cs[i].c01), c23 = as_bf2(cs[i].c23);
+    const __nv_bfloat162 s01 = as_bf2(cs[i].s01), s23 = as_bf2(cs[i].s23);
 #pragma unroll
     for (int h = 0; h < kHeads; ++h) {
       const float inv = rsqrtf(__fadd_rn(__fmul_rn(ss[i][h], 1.0f / kHeadDim), a.eps));
@@ -344,10 +344,12 @@ __global__ void __launch_bounds__(QkvCfg<kHeads>::kThreads, 1)
       const int head_row0 = (tile % groups_per_tok) * kHeads;
       const bool is_q = head_row0 < a.num_heads;
       const bool is_v = head_row0 >= a.num_heads + a.num_kv;
-      // Row facts for this tile, while the MMAs run (stage 2 of the previous tile has finished
-      // reading them: the barrier at the end of the previous iteration).
-      if (etid < Cfg::kTileRows) {
-        const long long t = m0 + etid;
+      // This warp's 8 stage-2 rows (8w .. 8w + 7): their facts (lanes 0-7, into shared memory)
+      // and, for query/key heads, their cos/sin at this lane's dims, loaded while the MMAs still
+      // run.  The warp's own facts were last read by this warp in the previous tile's stage 2.
+      const int row0 = warp * 8;
+      if (lane < 8) {
+        const long long t = m0 + row0 + lane;
         long long slot = -1, cs_row = 0;
         if (t < a.num_tokens) {
           slot = 0;
@@ -369,9 +371,24 @@ __global__ void __launch_bounds__(QkvCfg<kHeads>::kThreads, 1)
             }
           }
         }
-        asm volatile("st.shared.v2.b64 [%0], {%1, %2};" ::"r"(meta_base + etid * 16), "l"(slot),
-                     "l"(cs_row)
+        asm volatile("st.shared.v2.b64 [%0], {%1, %2};" ::"r"(meta_base + (row0 + lane) * 16),
+                     "l"(slot), "l"(cs_row)
                      : "memory");
+      }
+      __syncwarp();
+      RopeRow rope[8];
+      if (!is_v) {
+        float4 c4[8], s4[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const long long cs_row = ld_meta(meta_base + (row0 + i) * 16).cs_row;
+          c4[i] = *reinterpret_cast<const float4*>(a.cos + cs_row * a.cs_row_stride + lane * 4);
+          s4[i] = *reinterpret_cast<const float4*>(a.sin + cs_row * a.cs_row_stride + lane * 4);
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          rope[i] = RopeRow{pack_bf16(c4[i].x, c4[i].y), pack_bf16(c4[i].z, c4[i].w),
+                            pack_bf16(s4[i].x, s4[i].y), pack_bf16(s4[i].z, s4[i].w)};
       }
       // Stage 1: accumulator -> bf16 staging rows.  Every epilogue warp reports whether its
       // wait succeeded; all of them leave together if one did not.
@@ -379,28 +396,26 @@ __global__ void __launch_bounds__(QkvCfg<kHeads>::kThreads, 1)
           __all_sync(0xffffffffu, mbar_wait_fast(&acc_full[b], (j >> 1) & 1, abort_flag));
       tc_fence_after();
       if (mine) {
-        float v[kHeads][32];
-#pragma unroll
-        for (int h = 0; h < kHeads; ++h)
-          tmem_ld32(tmem + (static_cast<uint32_t>(quarter * 32) << 16) + b * Cfg::kTileN +
-                        h * 128 + colq * 32,
-                    v[h]);
-        tmem_wait_ld();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&acc_empty[b]);  // the MMA warp may reuse accumulator b
         const uint32_t row_addr = stage_base + (quarter * 32 + lane) * Cfg::kRowPitch + colq * 64;
 #pragma unroll
         for (int h = 0; h < kHeads; ++h) {
+          float v[32];
+          tmem_ld32(tmem + (static_cast<uint32_t>(quarter * 32) << 16) + b * Cfg::kTileN +
+                        h * 128 + colq * 32,
+                    v);
+          tmem_wait_ld();
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
-            const float* e = v[h] + u * 8;
+            const float* e = v + u * 8;
             asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(row_addr + h * 256 + u * 16),
                          "r"(pack_bf16(e[0], e[1])), "r"(pack_bf16(e[2], e[3])),
                          "r"(pack_bf16(e[4], e[5])), "r"(pack_bf16(e[6], e[7]))
                          : "memory");
           }
         }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[b]);  // the MMA warp may reuse accumulator b
       }
       if (lane == 0) verdict[warp] = mine ? 1 : 0;
       epi_bar_sync();
@@ -413,7 +428,6 @@ __global__ void __launch_bounds__(QkvCfg<kHeads>::kThreads, 1)
         break;
       }
       // Stage 2: kernel A on the staged rows; warp w takes rows 8w .. 8w + 7.
-      const int row0 = warp * 8;
       if (is_v) {
         const int h0 = head_row0 - a.num_heads - a.num_kv;
         __nv_bfloat16* vbase = a.k_pool + 2 * kBlockTokens * 64;
@@ -430,11 +444,11 @@ __global__ void __launch_bounds__(QkvCfg<kHeads>::kThreads, 1)
         }
       } else {
         const uint2 w2 = *reinterpret_cast<const uint2*>((is_q ? a.q_weight : a.k_weight) + lane * 4);
-        constexpr int kRows = 4 / kHeads;  // rows per batch of loads (register budget: 96)
+        constexpr int kRows = 4 / kHeads;  // rows per batch (register budget: 96)
 #pragma unroll
         for (int i = 0; i < 8; i += kRows)
           norm_rope_rows<kHeads, kRows>(a, stage_base, meta_base, row0 + i, m0, head_row0, is_q,
-                                        w2, lane);
+                                        w2, rope + i, lane);
       }
       epi_bar_sync();  // the staging tile and the row facts are free for the next tile
     }

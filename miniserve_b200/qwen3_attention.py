@@ -4,7 +4,8 @@ sm_100a kernels (src/miniserve/model/qwen3.py:65-100).
 The module keeps the reference's parameter names (``qkv_proj``, ``o_proj``, ``q_norm.weight``,
 ``k_norm.weight``) so the reference loader (``load_weights``, model/loader.py:51-79) fills it
 unchanged, and the same ``forward(x, cos, sin, k_cache, v_cache, meta)`` signature, so
-``Qwen3DecoderLayer`` calls it unchanged.  Only the two GEMMs stay library calls (cuBLAS).
+``Qwen3DecoderLayer`` calls it unchanged.  The o_proj GEMM stays a library call (cuBLAS); the qkv
+projection is cuBLAS followed by kernel A, or, with ``fused_qkv``, kernel E (both in one launch).
 """
 
 from __future__ import annotations
@@ -148,6 +149,10 @@ class Qwen3Attention(nn.Module):
         self.o_proj: nn.Module = nn.Linear(self.q_size, cfg.hidden_size, bias=False)
         self.q_norm = HeadNorm(self.head_dim, cfg.rms_norm_eps)
         self.k_norm = HeadNorm(self.head_dim, cfg.rms_norm_eps)
+        # True: kernel E computes the projection and the norm/RoPE/scatter in one launch (faster
+        # from a few thousand tokens per step; a projection output can differ from cuBLAS's by one
+        # bf16 ulp, from the GEMM's accumulation order).  False: cuBLAS, then kernel A.
+        self.fused_qkv = bool(getattr(cfg, "fused_qkv", False))
 
     def forward(
         self,
@@ -159,11 +164,17 @@ class Qwen3Attention(nn.Module):
         meta: AttentionMetadata,
     ) -> Tensor:
         t = x.shape[0]
-        qkv = self.qkv_proj(x)
-        q = qk_norm_rope_scatter(
-            qkv, self.q_norm.weight, self.k_norm.weight, self.q_norm.eps, cos, sin,
-            meta.slot_mapping, k_cache, v_cache, self.num_heads,
-        )
+        if self.fused_qkv and isinstance(self.qkv_proj, nn.Linear):
+            q = qkv_proj_norm_rope_scatter(
+                x, self.qkv_proj.weight, self.q_norm.weight, self.k_norm.weight, self.q_norm.eps,
+                cos, sin, meta.slot_mapping, k_cache, v_cache, self.num_heads,
+            )
+        else:
+            qkv = self.qkv_proj(x)
+            q = qk_norm_rope_scatter(
+                qkv, self.q_norm.weight, self.k_norm.weight, self.q_norm.eps, cos, sin,
+                meta.slot_mapping, k_cache, v_cache, self.num_heads,
+            )
         out = attend(q, k_cache, v_cache, meta, self.scale)
         result: Tensor = self.o_proj(out.reshape(t, self.q_size))
         return result

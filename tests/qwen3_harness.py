@@ -90,14 +90,16 @@ class Qwen3Weights:
 AttentionStep = Callable[[int, Tensor], Tensor]  # (layer, qkv [T, (H+2KVH)*D]) -> [T, H*D]
 
 
-def forward(w: Qwen3Weights, input_ids: Tensor, attention: AttentionStep) -> Tensor:
-    """Final hidden states [T, hidden] (qwen3.py:140-153)."""
+def forward(w: Qwen3Weights, input_ids: Tensor, attention: AttentionStep,
+            from_hidden: bool = False) -> Tensor:
+    """Final hidden states [T, hidden] (qwen3.py:140-153).  from_hidden: `attention` receives the
+    normalised hidden states and does the qkv projection itself (a fused projection kernel)."""
     s, t = w.s, w.t
     x = t["embed"][input_ids]
     for i in range(s.layers):
         h = orc.rms_norm(x, t[f"{i}.ln1"], s.eps)
-        qkv = F.linear(h, t[f"{i}.qkv"])
-        x = x + F.linear(attention(i, qkv), t[f"{i}.o"])
+        att_in = h if from_hidden else F.linear(h, t[f"{i}.qkv"])
+        x = x + F.linear(attention(i, att_in), t[f"{i}.o"])
         h = orc.rms_norm(x, t[f"{i}.ln2"], s.eps)
         gate, up = F.linear(h, t[f"{i}.gu"]).chunk(2, dim=-1)
         x = x + F.linear(F.silu(gate) * up, t[f"{i}.down"])

@@ -7,7 +7,8 @@ then a 300-token decode, an 80-token chunk over 100 cached tokens, a decode, and
 speculative verify; then decodes.  Three paths run the same weights and tokens:
   * ref32 -- the reference's op sequence (the oracle's attention) with everything in fp32;
   * ref16 -- the same in bf16, as MiniServe runs on a GPU (PyTorch ops on CUDA);
-  * ours  -- bf16, kernel A + kernels B/C/D through the C ABI over the B200 pool.
+  * ours  -- bf16, kernel A + kernels B/C/D through the C ABI over the B200 pool (parametrized:
+             the qkv projection by cuBLAS then kernel A, or kernel E doing both).
 All paths are fed the fp32 reference's greedy tokens, and the argmax of every row of every step
 is compared (about 535 rows).  In bf16 a near-tie can flip in any implementation, the reference's
 own included, so the bar is: ours picks the same token as ref16 on every row whose ref16
@@ -25,7 +26,7 @@ import torch
 
 from miniserve_b200.attention import SeqChunk, attend, build_attention_metadata
 from miniserve_b200.kv_pool import allocate_kv_cache
-from miniserve_b200.qwen3_attention import qk_norm_rope_scatter
+from miniserve_b200.qwen3_attention import qk_norm_rope_scatter, qkv_proj_norm_rope_scatter
 from oracle import attention_oracle as orc
 from qwen3_harness import QWEN3_06B, Qwen3Weights, forward, logits, oracle_attention
 
@@ -42,7 +43,7 @@ class Seq:
         self.table = table
 
 
-def _run_step(w, w32, plan, seqs, ref_kv, ref32_kv, pool_views, cos_t, sin_t, dev):
+def _run_step(w, w32, plan, seqs, ref_kv, ref32_kv, pool_views, cos_t, sin_t, dev, fused_qkv):
     """plan: list of (seq index, tokens to feed).  Returns (ref32, ref16, ours) logits of all rows."""
     s = w.s
     chunks_ref, chunks_ours, ids, pos, slots = [], [], [], [], []
@@ -65,20 +66,25 @@ def _run_step(w, w32, plan, seqs, ref_kv, ref32_kv, pool_views, cos_t, sin_t, de
 
     meta = build_attention_metadata(chunks_ours, slot_t, BLOCK)
 
-    def ours(i: int, qkv: torch.Tensor) -> torch.Tensor:
+    def ours(i: int, att_in: torch.Tensor) -> torch.Tensor:
         kc, vc = pool_views[i]
-        q = qk_norm_rope_scatter(qkv, w.t[f"{i}.qn"], w.t[f"{i}.kn"], s.eps, cos_rows, sin_rows,
-                                 slot_t, kc, vc, s.heads)
+        if fused_qkv:  # att_in = normalised hidden states; kernel E does the projection
+            q = qkv_proj_norm_rope_scatter(att_in, w.t[f"{i}.qkv"], w.t[f"{i}.qn"], w.t[f"{i}.kn"],
+                                           s.eps, cos_rows, sin_rows, slot_t, kc, vc, s.heads)
+        else:  # att_in = the projection output (cuBLAS); kernel A
+            q = qk_norm_rope_scatter(att_in, w.t[f"{i}.qn"], w.t[f"{i}.kn"], s.eps, cos_rows,
+                                     sin_rows, slot_t, kc, vc, s.heads)
         return attend(q, kc, vc, meta, s.head_dim**-0.5).reshape(len(ids), s.heads * s.head_dim)
 
-    our_hidden = forward(w, ids_t, ours)
+    our_hidden = forward(w, ids_t, ours, from_hidden=fused_qkv)
     for si, toks in plan:
         seqs[si].done += len(toks)
     return logits(w32, ref32_hidden), logits(w, ref_hidden), logits(w, our_hidden)
 
 
 @torch.no_grad()
-def test_greedy_tokens_identical_full_forward(cuda_device: torch.device) -> None:
+@pytest.mark.parametrize("fused_qkv", [False, True], ids=["cublas_qkv+kernel_a", "kernel_e"])
+def test_greedy_tokens_identical_full_forward(fused_qkv: bool, cuda_device: torch.device) -> None:
     dev = cuda_device
     w = Qwen3Weights.random(QWEN3_06B, seed=0, dtype=torch.bfloat16, device=dev)
     w.t["embed"] = (w.t["embed"].float() * 2.5).bfloat16()  # logits spread like a trained model's
@@ -109,7 +115,7 @@ def test_greedy_tokens_identical_full_forward(cuda_device: torch.device) -> None
         return r32.argmax(-1).tolist()
 
     def run(plan):
-        return _run_step(w, w32, plan, seqs, ref_kv, ref32_kv, views, cos_t, sin_t, dev)
+        return _run_step(w, w32, plan, seqs, ref_kv, ref32_kv, views, cos_t, sin_t, dev, fused_qkv)
 
     # step 1: prefills (B only its first 100 tokens)
     plan = [(0, prompts[0]), (1, prompts[1][:100]), (2, prompts[2]), (3, prompts[3])]

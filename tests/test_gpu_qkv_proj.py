@@ -153,3 +153,49 @@ def test_argument_checks(cuda_device) -> None:
     with pytest.raises(ValueError):  # hidden not a multiple of 64 (rejected by the C ABI)
         qkv_proj_norm_rope_scatter(x[:, :1000].contiguous().to(cuda_device),
                                    w[:, :1000].contiguous().to(cuda_device), *args)
+
+
+@pytest.mark.parametrize("kind", ["exact", "gaussian"])
+def test_drop_in_module_fused_flag(kind: str, cuda_device) -> None:
+    """Qwen3Attention (the reference's module shape) with fused_qkv on and off: equal outputs on
+    exact inputs, within the stated tolerance on gaussian ones."""
+    from types import SimpleNamespace
+
+    from miniserve_b200.attention import SeqChunk, build_attention_metadata
+    from miniserve_b200.qwen3_attention import Qwen3Attention
+
+    t, nb = 300, 40
+    x, w, qw, kw, positions, _ = _inputs(t, kind, seed=21, num_blocks=nb)
+    positions = torch.arange(t)  # one sequence's prefill
+    table = torch.randperm(nb, generator=torch.Generator().manual_seed(3)).tolist()
+    slots = torch.tensor([table[p // 16] * 16 + p % 16 for p in range(t)], dtype=torch.int64)
+    cos_t, sin_t = orc.rope_tables(D, 4096, THETA)
+    cos, sin = cos_t[positions].to(cuda_device), sin_t[positions].to(cuda_device)
+    outs = []
+    for fused in (False, True):
+        cfg = SimpleNamespace(num_attention_heads=H, num_key_value_heads=KVH, head_dim=D,
+                              hidden_size=HIDDEN, rms_norm_eps=EPS, fused_qkv=fused)
+        mod = Qwen3Attention(cfg).to(device=cuda_device, dtype=torch.bfloat16)
+        with torch.no_grad():
+            mod.qkv_proj.weight.copy_(w)
+            mod.o_proj.weight.copy_(
+                (torch.randn(HIDDEN, H * D, generator=torch.Generator().manual_seed(4)) / 64).bfloat16())
+            mod.q_norm.weight.copy_(qw)
+            mod.k_norm.weight.copy_(kw)
+        pool, views = allocate_kv_cache(1, nb, KVH, cuda_device)
+        slot_d = slots.to(cuda_device)
+        meta = build_attention_metadata([SeqChunk(0, t, 0, table)], slot_d, 16)
+        flag = torch.backends.cuda.matmul.allow_bf16_reduced_precision_reduction
+        torch.backends.cuda.matmul.allow_bf16_reduced_precision_reduction = False
+        try:
+            with torch.no_grad():
+                outs.append(mod(x.to(cuda_device), cos, sin, *views[0], meta))
+        finally:
+            torch.backends.cuda.matmul.allow_bf16_reduced_precision_reduction = flag
+        assert _capi.device_status(int(torch.cuda.current_stream(cuda_device).cuda_stream)) == 0
+    if kind == "exact":
+        assert torch.equal(outs[0], outs[1])
+    else:
+        ulps = bf16_ulp_diff(outs[0], outs[1])
+        assert (ulps <= 2).float().mean().item() >= 0.99
+        assert (outs[0].float() - outs[1].float()).abs().max().item() <= 0.05
