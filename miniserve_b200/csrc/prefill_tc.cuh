@@ -236,21 +236,28 @@ __global__ void __launch_bounds__(TcCfg::kThreads, 1)
     if (lane == 0) mbar_arrive(tmem_ready);
   }
   if (warp < 8) {
-    // Q tiles: thread r loads row r % 128 of tile r / 128 into the swizzled K-major layout.
-    const int t = threadIdx.x >> 7, r = threadIdx.x & 127;
-    const bool valid = (r >> 1) < (t == 0 ? n_a : n_b);
-    const int tok = (t == 0 ? tok_a : tok_b) + (r >> 1);
-    const __nv_bfloat16* src = a.q + static_cast<long long>(flat_start + tok) * a.q_row_stride +
-                               (kvh * kGroup + (r & 1)) * kHeadDim;
-    // All 16 loads are issued before any store: a shared store through a generic pointer between
-    // them would make each load wait for the previous one (possible aliasing), 16 round trips.
-    const uint32_t qs = smem_u32(smem + TcCfg::kQOff + t * TcCfg::kQBytes);
+    // Q tiles into the swizzled K-major layout: 256 rows (2 tiles x 64 tokens x 2 heads) of 16
+    // chunks of 16 bytes; each load instruction of a warp covers two whole rows (512 contiguous
+    // bytes: one token's two heads), so the loads coalesce.  All 16 loads are issued before any
+    // store (a shared store between them would make each load wait for the previous one).
     uint4 v[16];
 #pragma unroll
-    for (int u = 0; u < 16; ++u)
-      v[u] = valid ? __ldg(reinterpret_cast<const uint4*>(src) + u) : make_uint4(0u, 0u, 0u, 0u);
+    for (int i = 0; i < 16; ++i) {
+      const int f = i * 256 + threadIdx.x;
+      const int t = f >> 11, r = (f >> 4) & 127, u = f & 15;
+      const bool valid = (r >> 1) < (t == 0 ? n_a : n_b);
+      const int tok = (t == 0 ? tok_a : tok_b) + (r >> 1);
+      const __nv_bfloat16* src = a.q + static_cast<long long>(flat_start + tok) * a.q_row_stride +
+                                 (kvh * kGroup + (r & 1)) * kHeadDim + u * 8;
+      v[i] = valid ? __ldg(reinterpret_cast<const uint4*>(src)) : make_uint4(0u, 0u, 0u, 0u);
+    }
 #pragma unroll
-    for (int u = 0; u < 16; ++u) st_shared_v4(qs + tile128_off(r, u), v[u].x, v[u].y, v[u].z, v[u].w);
+    for (int i = 0; i < 16; ++i) {
+      const int f = i * 256 + threadIdx.x;
+      const int t = f >> 11, r = (f >> 4) & 127, u = f & 15;
+      st_shared_v4(smem_u32(smem + TcCfg::kQOff + t * TcCfg::kQBytes) + tile128_off(r, u), v[i].x,
+                   v[i].y, v[i].z, v[i].w);
+    }
     fence_proxy_async_smem();
     mbar_arrive(q_ready);
   }
