@@ -75,8 +75,8 @@ def _run(path: str, x, w, qw, kw, positions, slots, num_blocks: int, device, pos
     return q, layer_as_slots(k_cache), layer_as_slots(v_cache), status
 
 
-# 2400 and 4096 tokens reach the two-heads-per-tile form (enough tiles for two per SM); 2400
-# leaves a ragged last token block.
+# 1, 77, 128 and 300 tokens run the one-head-per-tile form; 1024, 2400 and 4096 the
+# two-heads-per-tile form (2400 leaves a ragged last token block).
 @pytest.mark.parametrize("t", [1, 77, 128, 300, 1024, 2400, 4096])
 def test_exact_inputs_bit_equal_to_cublas_plus_kernel_a(t: int, cuda_device) -> None:
     nb = (t + 15) // 16 + 8
