@@ -33,6 +33,18 @@ constexpr unsigned kErrPosition = 8u;  // a RoPE position outside the cos/sin ta
 // ~1e6 polls of try_wait with a 1 us suspend hint: about a second before giving up.
 constexpr int kSpinLimit = 1 << 20;
 
+// Programmatic dependent launch (sm_90 and later): every kernel of this library is launched with
+// programmatic stream serialization, so its grid may be scheduled while the previous kernel in
+// the stream is still running (hiding the launch gap between the per-layer kernels).  Each
+// kernel calls pdl_wait() before its first global-memory access -- it returns once the previous
+// grid has completed and its writes are visible -- then pdl_trigger(), which lets the next grid
+// be scheduled in turn (once every CTA of this grid has triggered or exited).  Both are hardware
+// dependencies, not spin-waits; without a programmatic predecessor pdl_wait() returns at once.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

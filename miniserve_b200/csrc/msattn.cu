@@ -10,6 +10,7 @@
 #include <mutex>
 #include <string>
 #include <unordered_map>
+#include <utility>
 
 #include "../../include/msattn.h"
 #include "ms_common.cuh"
@@ -134,6 +135,24 @@ static int matrix_tile_map(const void* base, int64_t rows, int64_t cols, int64_t
     return MS_ERR_CUDA;
   }
   return MS_OK;
+}
+
+// Every kernel is launched with programmatic stream serialization (see pdl_wait in
+// ms_common.cuh): its grid may start while the previous kernel in the stream finishes.
+template <typename... KArgs, typename... Args>
+static cudaError_t launch(void (*kernel)(KArgs...), unsigned grid, unsigned block, size_t smem,
+                          cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 // ---- attention launch configurations --------------------------------------------------------
@@ -360,9 +379,9 @@ extern "C" int ms_qk_norm_rope_scatter(const void* qkv, int64_t qkv_row_stride, 
     set_error("ms_qk_norm_rope_scatter: batch too large");
     return MS_ERR_ARG;
   }
-  ms::qk_norm_rope_scatter_kernel<kWarps>
-      <<<static_cast<unsigned>(blocks), kWarps * 32, 0, static_cast<cudaStream_t>(stream)>>>(a, st);
-  const cudaError_t e = cudaGetLastError();
+  const cudaError_t e = launch(ms::qk_norm_rope_scatter_kernel<kWarps>,
+                               static_cast<unsigned>(blocks), kWarps * 32, 0,
+                               static_cast<cudaStream_t>(stream), a, st);
   if (e != cudaSuccess) return cuda_fail("qk_norm_rope_scatter launch", e);
   return MS_OK;
 }
@@ -449,13 +468,11 @@ extern "C" int ms_qkv_proj_norm_rope_scatter(
   qa.num_tiles = static_cast<int>(m_tiles * (pairs ? rows / 2 : rows));
   const int grid = qa.num_tiles < sms ? qa.num_tiles : sms;  // persistent: one CTA per SM
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (pairs)
-    ms::qkv_proj_norm_rope_kernel<2>
-        <<<grid, ms::QkvCfg<2>::kThreads, ms::QkvCfg<2>::kSmemBytes, s>>>(xmap, wmap, qa, st);
-  else
-    ms::qkv_proj_norm_rope_kernel<1>
-        <<<grid, ms::QkvCfg<1>::kThreads, ms::QkvCfg<1>::kSmemBytes, s>>>(xmap, wmap, qa, st);
-  const cudaError_t e = cudaGetLastError();
+  const cudaError_t e =
+      pairs ? launch(ms::qkv_proj_norm_rope_kernel<2>, grid, ms::QkvCfg<2>::kThreads,
+                     ms::QkvCfg<2>::kSmemBytes, s, xmap, wmap, qa, st)
+            : launch(ms::qkv_proj_norm_rope_kernel<1>, grid, ms::QkvCfg<1>::kThreads,
+                     ms::QkvCfg<1>::kSmemBytes, s, xmap, wmap, qa, st);
   if (e != cudaSuccess) return cuda_fail("qkv_proj_norm_rope launch", e);
   return MS_OK;
 }
@@ -494,9 +511,8 @@ extern "C" int ms_kv_scatter(const void* k, int64_t k_row_stride, const void* v,
   constexpr int kWarps = 8;
   const long long warps = static_cast<long long>(num_tokens) * 2 * num_kv_heads;
   const long long blocks = (warps + kWarps - 1) / kWarps;
-  ms::kv_scatter_kernel<kWarps>
-      <<<static_cast<unsigned>(blocks), kWarps * 32, 0, static_cast<cudaStream_t>(stream)>>>(a, st);
-  const cudaError_t e = cudaGetLastError();
+  const cudaError_t e = launch(ms::kv_scatter_kernel<kWarps>, static_cast<unsigned>(blocks),
+                               kWarps * 32, 0, static_cast<cudaStream_t>(stream), a, st);
   if (e != cudaSuccess) return cuda_fail("kv_scatter launch", e);
   return MS_OK;
 }
@@ -587,9 +603,8 @@ extern "C" int ms_paged_attention(const void* q, int64_t q_row_stride, void* out
   if (plan->n_tc_items > 0) {
     a.items = plan_dev + plan->off_tc;
     a.n_items = plan->n_tc_items;
-    ms::prefill_tc_kernel<<<plan->n_tc_items * num_kv_heads, ms::TcCfg::kThreads,
-                            ms::TcCfg::kSmemBytes, s>>>(kmap, vmap, a);
-    const cudaError_t e = cudaGetLastError();
+    const cudaError_t e = launch(ms::prefill_tc_kernel, plan->n_tc_items * num_kv_heads,
+                                 ms::TcCfg::kThreads, ms::TcCfg::kSmemBytes, s, kmap, vmap, a);
     if (e != cudaSuccess) {
       join();
       return cuda_fail("prefill_tc launch", e);
@@ -598,9 +613,9 @@ extern "C" int ms_paged_attention(const void* q, int64_t q_row_stride, void* out
   if (plan->n_decode_items > 0) {
     a.items = plan_dev + plan->off_decode;
     a.n_items = plan->n_decode_items;
-    ms::paged_attn_kernel<0, kDecodeWarps, kDecodeStages>
-        <<<plan->n_decode_items * num_kv_heads, DecodeCfg::kThreads, DecodeCfg::kSmemBytes, ds>>>(map, a);
-    const cudaError_t e = cudaGetLastError();
+    const cudaError_t e = launch(ms::paged_attn_kernel<0, kDecodeWarps, kDecodeStages>,
+                                 plan->n_decode_items * num_kv_heads, DecodeCfg::kThreads,
+                                 DecodeCfg::kSmemBytes, ds, map, a);
     if (e != cudaSuccess) {
       join();
       return cuda_fail("paged_attn decode launch", e);
@@ -609,9 +624,9 @@ extern "C" int ms_paged_attention(const void* q, int64_t q_row_stride, void* out
   if (plan->n_tile_items > 0) {
     a.items = plan_dev + plan->off_tile;
     a.n_items = plan->n_tile_items;
-    ms::paged_attn_kernel<1, kTileWarps, kTileStages>
-        <<<plan->n_tile_items * num_kv_heads, TileCfg::kThreads, TileCfg::kSmemBytes, s>>>(map, a);
-    const cudaError_t e = cudaGetLastError();
+    const cudaError_t e = launch(ms::paged_attn_kernel<1, kTileWarps, kTileStages>,
+                                 plan->n_tile_items * num_kv_heads, TileCfg::kThreads,
+                                 TileCfg::kSmemBytes, s, map, a);
     if (e != cudaSuccess) {
       join();
       return cuda_fail("paged_attn tile launch", e);
@@ -631,8 +646,8 @@ extern "C" int ms_paged_attention(const void* q, int64_t q_row_stride, void* out
     c.num_kv = num_kv_heads;
     c.ws_o = a.ws_o;
     c.ws_lse = a.ws_lse;
-    ms::combine_kernel<<<plan->n_combine * num_kv_heads, ms::kCombineThreads, 0, s>>>(c);
-    const cudaError_t e = cudaGetLastError();
+    const cudaError_t e =
+        launch(ms::combine_kernel, plan->n_combine * num_kv_heads, ms::kCombineThreads, 0, s, c);
     if (e != cudaSuccess) return cuda_fail("combine launch", e);
   }
   return MS_OK;

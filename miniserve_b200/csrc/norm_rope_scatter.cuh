@@ -64,6 +64,8 @@ constexpr int kRowsPerWarp = 8;
 template <int kWarps>
 __global__ void __launch_bounds__(kWarps * 32)
     qk_norm_rope_scatter_kernel(const NormRopeArgs a, unsigned* status) {
+  pdl_wait();
+  pdl_trigger();
   const int lane = threadIdx.x & 31;
   const int warps_per_tok = (a.num_heads + 2 * a.num_kv) / kRowsPerWarp;
   const long long gw = static_cast<long long>(blockIdx.x) * kWarps + (threadIdx.x >> 5);
@@ -179,6 +181,8 @@ struct ScatterArgs {
 template <int kWarps>
 __global__ void __launch_bounds__(kWarps * 32) kv_scatter_kernel(const ScatterArgs a,
                                                                  unsigned* status) {
+  pdl_wait();
+  pdl_trigger();
   const int lane = threadIdx.x & 31;
   const long long gw = static_cast<long long>(blockIdx.x) * kWarps + (threadIdx.x >> 5);
   const long long t = gw / (2 * a.num_kv);

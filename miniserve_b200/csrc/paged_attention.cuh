@@ -155,6 +155,8 @@ __device__ unsigned g_status_word;  // device status bits (kErr*), read by ms_de
 template <int kMode, int kConsumerWarps, int kStages>
 __global__ void __launch_bounds__(AttnCfg<kMode, kConsumerWarps, kStages>::kThreads)
     paged_attn_kernel(const __grid_constant__ CUtensorMap kv_map, const AttnArgs a) {
+  pdl_wait();
+  pdl_trigger();
   using Cfg = AttnCfg<kMode, kConsumerWarps, kStages>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -475,6 +477,8 @@ struct CombineArgs {
 // One CTA per (split tile, KV head); thread = (row, 16-dim slice), 32 rows per pass.
 constexpr int kCombineThreads = 256;
 __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const CombineArgs a) {
+  pdl_wait();
+  pdl_trigger();
   const int ci = blockIdx.x / a.num_kv;
   const int kvh = blockIdx.x - ci * a.num_kv;
   const int* cr = a.combines + static_cast<long long>(ci) * kRec;

@@ -163,6 +163,8 @@ __device__ __forceinline__ void exp_pack32(const float (&sv)[32], float2 sc2, fl
 __global__ void __launch_bounds__(TcCfg::kThreads, 1)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap k_map,
                       const __grid_constant__ CUtensorMap v_map, const AttnArgs a) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));

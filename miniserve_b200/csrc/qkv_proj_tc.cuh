@@ -210,6 +210,8 @@ __global__ void __launch_bounds__(QkvCfg<kHeads>::kThreads, 1)
     qkv_proj_norm_rope_kernel(const __grid_constant__ CUtensorMap x_map,
                               const __grid_constant__ CUtensorMap w_map, const QkvArgs qa,
                               unsigned* status) {
+  pdl_wait();
+  pdl_trigger();
   using Cfg = QkvCfg<kHeads>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
