@@ -176,9 +176,15 @@ static int ensure_smem_attrs() {
   e = cudaFuncSetAttribute(ms::paged_attn_kernel<0, kDecodeWarps, kDecodeStages>,
                            cudaFuncAttributeMaxDynamicSharedMemorySize, DecodeCfg::kSmemBytes);
   if (e != cudaSuccess) return cuda_fail("cudaFuncSetAttribute(decode)", e);
+  e = cudaFuncSetAttribute(ms::paged_attn_kernel<0, kDecodeWarps, kDecodeStages, true>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, DecodeCfg::kSmemBytes);
+  if (e != cudaSuccess) return cuda_fail("cudaFuncSetAttribute(decode, early)", e);
   e = cudaFuncSetAttribute(ms::paged_attn_kernel<1, kTileWarps, kTileStages>,
                            cudaFuncAttributeMaxDynamicSharedMemorySize, TileCfg::kSmemBytes);
   if (e != cudaSuccess) return cuda_fail("cudaFuncSetAttribute(tile)", e);
+  e = cudaFuncSetAttribute(ms::paged_attn_kernel<1, kTileWarps, kTileStages, true>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, TileCfg::kSmemBytes);
+  if (e != cudaSuccess) return cuda_fail("cudaFuncSetAttribute(tile, early)", e);
   e = cudaFuncSetAttribute(ms::prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            ms::TcCfg::kSmemBytes);
   if (e != cudaSuccess) return cuda_fail("cudaFuncSetAttribute(tc)", e);
@@ -610,12 +616,24 @@ extern "C" int ms_paged_attention(const void* q, int64_t q_row_stride, void* out
       return cuda_fail("prefill_tc launch", e);
     }
   }
+  int sms = 0;
+  rc = sm_count(&sms);
+  if (rc) {
+    join();
+    return rc;
+  }
   if (plan->n_decode_items > 0) {
     a.items = plan_dev + plan->off_decode;
     a.n_items = plan->n_decode_items;
-    const cudaError_t e = launch(ms::paged_attn_kernel<0, kDecodeWarps, kDecodeStages>,
-                                 plan->n_decode_items * num_kv_heads, DecodeCfg::kThreads,
-                                 DecodeCfg::kSmemBytes, ds, map, a);
+    // One resident wave (two decode CTAs per SM): latency-bound, so stream earlier steps' pages
+    // while the previous kernel finishes.
+    const int ctas = plan->n_decode_items * num_kv_heads;
+    const cudaError_t e =
+        ctas <= 2 * sms
+            ? launch(ms::paged_attn_kernel<0, kDecodeWarps, kDecodeStages, true>, ctas,
+                     DecodeCfg::kThreads, DecodeCfg::kSmemBytes, ds, map, a)
+            : launch(ms::paged_attn_kernel<0, kDecodeWarps, kDecodeStages>, ctas,
+                     DecodeCfg::kThreads, DecodeCfg::kSmemBytes, ds, map, a);
     if (e != cudaSuccess) {
       join();
       return cuda_fail("paged_attn decode launch", e);
@@ -624,9 +642,12 @@ extern "C" int ms_paged_attention(const void* q, int64_t q_row_stride, void* out
   if (plan->n_tile_items > 0) {
     a.items = plan_dev + plan->off_tile;
     a.n_items = plan->n_tile_items;
-    const cudaError_t e = launch(ms::paged_attn_kernel<1, kTileWarps, kTileStages>,
-                                 plan->n_tile_items * num_kv_heads, TileCfg::kThreads,
-                                 TileCfg::kSmemBytes, s, map, a);
+    const int ctas = plan->n_tile_items * num_kv_heads;
+    const cudaError_t e =
+        ctas <= sms ? launch(ms::paged_attn_kernel<1, kTileWarps, kTileStages, true>, ctas,
+                             TileCfg::kThreads, TileCfg::kSmemBytes, s, map, a)
+                    : launch(ms::paged_attn_kernel<1, kTileWarps, kTileStages>, ctas,
+                             TileCfg::kThreads, TileCfg::kSmemBytes, s, map, a);
     if (e != cudaSuccess) {
       join();
       return cuda_fail("paged_attn tile launch", e);

@@ -152,10 +152,20 @@ __device__ __forceinline__ void attend_page(uint32_t stage, const uint32_t (&qf)
 
 __device__ unsigned g_status_word;  // device status bits (kErr*), read by ms_device_status
 
-template <int kMode, int kConsumerWarps, int kStages>
+// kEarly: the launch fits one resident wave (latency-bound); see the programmatic dependent
+// launch note at the top of the kernel.
+template <int kMode, int kConsumerWarps, int kStages, bool kEarly = false>
 __global__ void __launch_bounds__(AttnCfg<kMode, kConsumerWarps, kStages>::kThreads)
     paged_attn_kernel(const __grid_constant__ CUtensorMap kv_map, const AttnArgs a) {
-  pdl_wait();
+  // Programmatic dependent launch.  A launch that fits one resident wave (kEarly) is
+  // latency-bound: its producer reads the plan (copied in before the previous kernel started)
+  // and streams the pool pages holding only tokens cached in earlier steps before pdl_wait(),
+  // and the consumers wait before loading the queries; this step's K/V rows (written by the
+  // previous kernel) and every write come after the wait.  Only kernels of this library run as
+  // a programmatic predecessor, and none of them writes an earlier step's pages.  Any other
+  // launch waits at once: for a bandwidth-bound launch the early start only competes with the
+  // kernel it overlaps (measured 1-2 % slower on config 2).
+  if constexpr (!kEarly) pdl_wait();
   pdl_trigger();
   using Cfg = AttnCfg<kMode, kConsumerWarps, kStages>;
   extern __shared__ uint8_t smem_raw[];
@@ -195,6 +205,7 @@ __global__ void __launch_bounds__(AttnCfg<kMode, kConsumerWarps, kStages>::kThre
   // the query tile meanwhile and synchronise among themselves (named barrier 1).
   __syncthreads();
   if (warp < kConsumerWarps) {
+    if constexpr (kEarly) pdl_wait();
     // Query tile -> shared memory, swizzled like a page: [16-row group][d/64][row][d%64].  All of
     // a thread's loads are issued before its shared stores (a store between them would make each
     // load wait for the previous one).
@@ -232,6 +243,9 @@ __global__ void __launch_bounds__(AttnCfg<kMode, kConsumerWarps, kStages>::kThre
     const uint64_t policy = l2_policy_evict_first();
     if (lane == 0) tma_prefetch_desc(&kv_map);
     const int* table = a.tables + table_off + page_begin;
+    // Pages from here on may hold this step's new tokens (positions >= num_cached).
+    const int first_new = kEarly ? num_cached / kBlockTokens - page_begin : 0;
+    bool waited = !kEarly;
     int issued = 0;
     bool stop = false;
     for (int j0 = 0; j0 < npages && !stop; j0 += 32) {
@@ -240,6 +254,12 @@ __global__ void __launch_bounds__(AttnCfg<kMode, kConsumerWarps, kStages>::kThre
       const int cnt = min(32, npages - j0);
       for (int jj = 0; jj < cnt; ++jj) {
         const int blk = __shfl_sync(0xffffffffu, mine, jj);
+        if constexpr (kEarly) {
+          if (!waited && j0 + jj >= first_new) {
+            pdl_wait();
+            waited = true;
+          }
+        }
         int ok = 1;
         if (lane == 0) {
           const int j = j0 + jj;
