@@ -88,7 +88,8 @@ typedef struct MsPlanInfo {
                               once (tensor-core items over the group's tokens) and merge it with
                               their own pages; sequence records num_seqs .. num_seqs+n_cascade-1
                               describe the groups */
-  int32_t reserved[5];
+  int32_t decode_pages;    /* pages (per KV head) the decode / verify items read, in total */
+  int32_t reserved[4];
 } MsPlanInfo;
 
 /* Upper bound on the packed buffer length (int32 elements) for a batch of this size. */

@@ -61,7 +61,8 @@ class MsPlanInfo(C.Structure):
         ("n_tc_items", C.c_int32),
         ("off_tc", C.c_int32),
         ("n_cascade", C.c_int32),
-        ("reserved", C.c_int32 * 5),
+        ("decode_pages", C.c_int32),
+        ("reserved", C.c_int32 * 4),
     ]
 
 

@@ -161,6 +161,10 @@ constexpr int kDecodeWarps = 4, kDecodeStages = 8;
 constexpr int kTileWarps = 8, kTileStages = 8;
 using DecodeCfg = ms::AttnCfg<0, kDecodeWarps, kDecodeStages>;
 using TileCfg = ms::AttnCfg<1, kTileWarps, kTileStages>;
+using UnitsCfg = ms::UnitsCfg<kDecodeWarps, kDecodeStages>;
+// Decode launches of more than one resident wave whose items read at most this many pages on
+// average run persistent over work units (see paged_decode_units_kernel).
+constexpr int kUnitsMaxAvgPages = 32;
 static_assert(ms::TcCfg::kSmemBytes <= 232448, "tensor-core kernel exceeds 227 KiB of smem");
 
 static int ensure_smem_attrs() {
@@ -182,6 +186,9 @@ static int ensure_smem_attrs() {
   e = cudaFuncSetAttribute(ms::paged_attn_kernel<1, kTileWarps, kTileStages>,
                            cudaFuncAttributeMaxDynamicSharedMemorySize, TileCfg::kSmemBytes);
   if (e != cudaSuccess) return cuda_fail("cudaFuncSetAttribute(tile)", e);
+  e = cudaFuncSetAttribute(ms::paged_decode_units_kernel<kDecodeWarps, kDecodeStages>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, UnitsCfg::kSmemBytes);
+  if (e != cudaSuccess) return cuda_fail("cudaFuncSetAttribute(decode units)", e);
   e = cudaFuncSetAttribute(ms::paged_attn_kernel<1, kTileWarps, kTileStages, true>,
                            cudaFuncAttributeMaxDynamicSharedMemorySize, TileCfg::kSmemBytes);
   if (e != cudaSuccess) return cuda_fail("cudaFuncSetAttribute(tile, early)", e);
@@ -628,12 +635,19 @@ extern "C" int ms_paged_attention(const void* q, int64_t q_row_stride, void* out
     // One resident wave (two decode CTAs per SM): latency-bound, so stream earlier steps' pages
     // while the previous kernel finishes.
     const int ctas = plan->n_decode_items * num_kv_heads;
-    const cudaError_t e =
-        ctas <= 2 * sms
-            ? launch(ms::paged_attn_kernel<0, kDecodeWarps, kDecodeStages, true>, ctas,
-                     DecodeCfg::kThreads, DecodeCfg::kSmemBytes, ds, map, a)
-            : launch(ms::paged_attn_kernel<0, kDecodeWarps, kDecodeStages>, ctas,
-                     DecodeCfg::kThreads, DecodeCfg::kSmemBytes, ds, map, a);
+    cudaError_t e;
+    if (ctas <= 2 * sms) {
+      e = launch(ms::paged_attn_kernel<0, kDecodeWarps, kDecodeStages, true>, ctas,
+                 DecodeCfg::kThreads, DecodeCfg::kSmemBytes, ds, map, a);
+    } else if (static_cast<int64_t>(plan->decode_pages) <=
+               static_cast<int64_t>(kUnitsMaxAvgPages) * plan->n_decode_items) {
+      // Many short items: two persistent CTAs per SM walk the work units.
+      e = launch(ms::paged_decode_units_kernel<kDecodeWarps, kDecodeStages>, 2 * sms,
+                 UnitsCfg::kThreads, UnitsCfg::kSmemBytes, ds, map, a);
+    } else {
+      e = launch(ms::paged_attn_kernel<0, kDecodeWarps, kDecodeStages>, ctas,
+                 DecodeCfg::kThreads, DecodeCfg::kSmemBytes, ds, map, a);
+    }
     if (e != cudaSuccess) {
       join();
       return cuda_fail("paged_attn decode launch", e);

@@ -152,6 +152,113 @@ __device__ __forceinline__ void attend_page(uint32_t stage, const uint32_t (&qf)
 
 __device__ unsigned g_status_word;  // device status bits (kErr*), read by ms_device_status
 
+// Decode mode: merge the consumer warps' (m, l, O) over their page subsets through `merge`
+// (kConsumerWarps x 16 x (128 + 4) fp32 accumulators, then kConsumerWarps x 16 maxima and as many
+// sums) and write the rows: bf16 output (merged with a cascade row's shared-prefix partial when
+// merge_row >= 0) or fp32 partial rows and log2-sum-exp for split items.  Called by every
+// consumer thread (threadIdx.x < 32 * kConsumerWarps); uses named barrier 1.
+template <int kConsumerWarps>
+__device__ __forceinline__ void decode_merge_store(float* merge, const float (&o)[16][4],
+                                                   const float (&m)[2], const float (&l)[2],
+                                                   int warp, int lane, int n_q, int kvh,
+                                                   int part_row, int merge_row, int flat_start,
+                                                   int tok0, const AttnArgs& a) {
+  float* mo = merge;
+  float* mm = mo + kConsumerWarps * 16 * (kHeadDim + 4);
+  float* ml = mm + kConsumerWarps * 16;
+  asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
+  {
+    float* wo = mo + warp * 16 * (kHeadDim + 4);
+    const int ra = lane >> 2, rb = ra + 8, c = 2 * (lane & 3);
+#pragma unroll
+    for (int n = 0; n < 16; ++n) {
+      *reinterpret_cast<float2*>(wo + ra * (kHeadDim + 4) + n * 8 + c) = make_float2(o[n][0], o[n][1]);
+      *reinterpret_cast<float2*>(wo + rb * (kHeadDim + 4) + n * 8 + c) = make_float2(o[n][2], o[n][3]);
+    }
+    if ((lane & 3) == 0) {
+      mm[warp * 16 + ra] = m[0];
+      mm[warp * 16 + rb] = m[1];
+      ml[warp * 16 + ra] = l[0];
+      ml[warp * 16 + rb] = l[1];
+    }
+  }
+  asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
+  const int tid = threadIdx.x;
+  for (int e = tid; e < 16 * 8; e += kConsumerWarps * 32) {
+    const int r = e >> 3;
+    const int dc = (e & 7) * 16;
+    const int tok = r >> 1;
+    if (tok >= n_q) continue;
+    float mx = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kConsumerWarps; ++w) mx = fmaxf(mx, mm[w * 16 + r]);
+    float wsc[kConsumerWarps];
+    float L = 0.f;
+#pragma unroll
+    for (int w = 0; w < kConsumerWarps; ++w) {
+      const float mw = mm[w * 16 + r];
+      wsc[w] = mw == -INFINITY ? 0.f : fast_exp2(mw - mx);
+      L += ml[w * 16 + r] * wsc[w];
+    }
+    const float invL = L > 0.f ? 1.f / L : 0.f;
+    float acc[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) acc[i] = 0.f;
+#pragma unroll
+    for (int w = 0; w < kConsumerWarps; ++w) {
+      const float* src = mo + (w * 16 + r) * (kHeadDim + 4) + dc;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) acc[i] += src[i] * wsc[w];
+    }
+    const int head = kvh * kGroup + (r & 1);
+    if (part_row < 0) {
+      __nv_bfloat16* dst = a.out + static_cast<long long>(flat_start + tok0 + tok) * a.out_row_stride +
+                           head * kHeadDim + dc;
+      float scale_u = invL;  // weight of this item's own (unnormalised) accumulator
+      float wp = 0.f;        // weight of the merged shared-prefix partial
+      const float* op = nullptr;
+      if (merge_row >= 0) {
+        // Cascade row: merge the shared-prefix partial (normalised O and log2-sum-exp) that the
+        // tensor-core kernel wrote before this launch: out = (acc 2^(mx-M) + O_p L_p') / (...).
+        const long long prow = static_cast<long long>(merge_row + r) * a.num_kv + kvh;
+        const float lse_p = a.ws_lse[prow];
+        const float lse_u = L > 0.f ? mx + __log2f(L) : -INFINITY;
+        const float M = fmaxf(lse_u, lse_p);
+        const float wu = lse_u == -INFINITY ? 0.f : fast_exp2(lse_u - M);
+        wp = lse_p == -INFINITY ? 0.f : fast_exp2(lse_p - M);
+        const float inv = wu + wp > 0.f ? 1.f / (wu + wp) : 0.f;
+        scale_u = invL * wu * inv;
+        wp *= inv;
+        op = a.ws_o + prow * kHeadDim + dc;
+      }
+      if (op != nullptr) {
+#pragma unroll
+        for (int i = 0; i < 16; i += 4) {
+          const float4 pv = *reinterpret_cast<const float4*>(op + i);
+          acc[i] = acc[i] * scale_u + pv.x * wp;
+          acc[i + 1] = acc[i + 1] * scale_u + pv.y * wp;
+          acc[i + 2] = acc[i + 2] * scale_u + pv.z * wp;
+          acc[i + 3] = acc[i + 3] * scale_u + pv.w * wp;
+        }
+        scale_u = 1.f;
+      }
+      uint32_t pk[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) pk[i] = pack_bf16(acc[2 * i] * scale_u, acc[2 * i + 1] * scale_u);
+      reinterpret_cast<uint4*>(dst)[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      reinterpret_cast<uint4*>(dst)[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+    } else {
+      const long long prow = static_cast<long long>(part_row + r) * a.num_kv + kvh;
+      float* dst = a.ws_o + prow * kHeadDim + dc;
+#pragma unroll
+      for (int i = 0; i < 16; i += 4)
+        *reinterpret_cast<float4*>(dst + i) =
+            make_float4(acc[i] * invL, acc[i + 1] * invL, acc[i + 2] * invL, acc[i + 3] * invL);
+      if (dc == 0) a.ws_lse[prow] = L > 0.f ? mx + __log2f(L) : -INFINITY;
+    }
+  }
+}
+
 // kEarly: the launch fits one resident wave (latency-bound); see the programmatic dependent
 // launch note at the top of the kernel.
 template <int kMode, int kConsumerWarps, int kStages, bool kEarly = false>
@@ -357,100 +464,8 @@ __global__ void __launch_bounds__(AttnCfg<kMode, kConsumerWarps, kStages>::kThre
 
   if constexpr (kMode == 0) {
     // Cross-warp merge of the per-warp page subsets, through the (now idle) stage ring.
-    float* mo = reinterpret_cast<float*>(ring);
-    float* mm = mo + kConsumerWarps * 16 * (kHeadDim + 4);
-    float* ml = mm + kConsumerWarps * 16;
-    asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
-    {
-      float* wo = mo + warp * 16 * (kHeadDim + 4);
-      const int ra = lane >> 2, rb = ra + 8, c = 2 * (lane & 3);
-#pragma unroll
-      for (int n = 0; n < 16; ++n) {
-        *reinterpret_cast<float2*>(wo + ra * (kHeadDim + 4) + n * 8 + c) = make_float2(o[n][0], o[n][1]);
-        *reinterpret_cast<float2*>(wo + rb * (kHeadDim + 4) + n * 8 + c) = make_float2(o[n][2], o[n][3]);
-      }
-      if ((lane & 3) == 0) {
-        mm[warp * 16 + ra] = m[0];
-        mm[warp * 16 + rb] = m[1];
-        ml[warp * 16 + ra] = l[0];
-        ml[warp * 16 + rb] = l[1];
-      }
-    }
-    asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
-    const int tid = threadIdx.x;
-    for (int e = tid; e < 16 * 8; e += kConsumerWarps * 32) {
-      const int r = e >> 3;
-      const int dc = (e & 7) * 16;
-      const int tok = r >> 1;
-      if (tok >= n_q) continue;
-      float mx = -INFINITY;
-#pragma unroll
-      for (int w = 0; w < kConsumerWarps; ++w) mx = fmaxf(mx, mm[w * 16 + r]);
-      float wsc[kConsumerWarps];
-      float L = 0.f;
-#pragma unroll
-      for (int w = 0; w < kConsumerWarps; ++w) {
-        const float mw = mm[w * 16 + r];
-        wsc[w] = mw == -INFINITY ? 0.f : fast_exp2(mw - mx);
-        L += ml[w * 16 + r] * wsc[w];
-      }
-      const float invL = L > 0.f ? 1.f / L : 0.f;
-      float acc[16];
-#pragma unroll
-      for (int i = 0; i < 16; ++i) acc[i] = 0.f;
-#pragma unroll
-      for (int w = 0; w < kConsumerWarps; ++w) {
-        const float* src = mo + (w * 16 + r) * (kHeadDim + 4) + dc;
-#pragma unroll
-        for (int i = 0; i < 16; ++i) acc[i] += src[i] * wsc[w];
-      }
-      const int head = kvh * kGroup + (r & 1);
-      if (part_row < 0) {
-        __nv_bfloat16* dst = a.out + static_cast<long long>(flat_start + tok0 + tok) * a.out_row_stride +
-                             head * kHeadDim + dc;
-        float scale_u = invL;  // weight of this item's own (unnormalised) accumulator
-        float wp = 0.f;        // weight of the merged shared-prefix partial
-        const float* op = nullptr;
-        if (merge_row >= 0) {
-          // Cascade row: merge the shared-prefix partial (normalised O and log2-sum-exp) that the
-          // tensor-core kernel wrote before this launch: out = (acc 2^(mx-M) + O_p L_p') / (...).
-          const long long prow = static_cast<long long>(merge_row + r) * a.num_kv + kvh;
-          const float lse_p = a.ws_lse[prow];
-          const float lse_u = L > 0.f ? mx + __log2f(L) : -INFINITY;
-          const float M = fmaxf(lse_u, lse_p);
-          const float wu = lse_u == -INFINITY ? 0.f : fast_exp2(lse_u - M);
-          wp = lse_p == -INFINITY ? 0.f : fast_exp2(lse_p - M);
-          const float inv = wu + wp > 0.f ? 1.f / (wu + wp) : 0.f;
-          scale_u = invL * wu * inv;
-          wp *= inv;
-          op = a.ws_o + prow * kHeadDim + dc;
-        }
-        if (op != nullptr) {
-#pragma unroll
-          for (int i = 0; i < 16; i += 4) {
-            const float4 pv = *reinterpret_cast<const float4*>(op + i);
-            acc[i] = acc[i] * scale_u + pv.x * wp;
-            acc[i + 1] = acc[i + 1] * scale_u + pv.y * wp;
-            acc[i + 2] = acc[i + 2] * scale_u + pv.z * wp;
-            acc[i + 3] = acc[i + 3] * scale_u + pv.w * wp;
-          }
-          scale_u = 1.f;
-        }
-        uint32_t pk[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) pk[i] = pack_bf16(acc[2 * i] * scale_u, acc[2 * i + 1] * scale_u);
-        reinterpret_cast<uint4*>(dst)[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-        reinterpret_cast<uint4*>(dst)[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
-      } else {
-        const long long prow = static_cast<long long>(part_row + r) * a.num_kv + kvh;
-        float* dst = a.ws_o + prow * kHeadDim + dc;
-#pragma unroll
-        for (int i = 0; i < 16; i += 4)
-          *reinterpret_cast<float4*>(dst + i) =
-              make_float4(acc[i] * invL, acc[i + 1] * invL, acc[i + 2] * invL, acc[i + 3] * invL);
-        if (dc == 0) a.ws_lse[prow] = L > 0.f ? mx + __log2f(L) : -INFINITY;
-      }
-    }
+    decode_merge_store<kConsumerWarps>(reinterpret_cast<float*>(ring), o, m, l, warp, lane, n_q,
+                                       kvh, part_row, merge_row, flat_start, tok0, a);
   } else {
     if (!warp_active) return;
     const int c = 2 * (lane & 3);
@@ -479,6 +494,221 @@ __global__ void __launch_bounds__(AttnCfg<kMode, kConsumerWarps, kStages>::kThre
         if ((lane & 3) == 0) a.ws_lse[prow] = L > 0.f ? m[half] + __log2f(L) : -INFINITY;
       }
     }
+  }
+}
+
+// Decode mode, persistent over work units (unit u = (item u / num_kv, KV head u % num_kv); CTA c
+// takes units c, c + G, c + 2G, ...) for plans of many short items, where a one-unit CTA spends
+// most of its life starting up and finishing: here the producer streams the next unit's pages
+// while the consumers finish the current one, and each unit's query rows are loaded into
+// registers during the previous unit.  Per unit the consumer work is kernel B's decode mode (the
+// same attend_page and decode_merge_store), so the results are the same bit for bit; the merge
+// scratch has its own shared memory because the ring keeps streaming.
+template <int kConsumerWarps, int kStages>
+struct UnitsCfg {
+  using Base = AttnCfg<0, kConsumerWarps, kStages>;
+  static constexpr int kThreads = Base::kThreads;
+  static constexpr int kStageBytes = Base::kStageBytes;
+  static constexpr int kQBytes = Base::kQBytes;
+  static constexpr int kMergeOff = kStageBytes + kQBytes;
+  static constexpr int kMergeBytes = kConsumerWarps * 16 * (kHeadDim + 4) * 4 + 2 * kConsumerWarps * 16 * 4;
+  static constexpr int kBarOffset = kMergeOff + kMergeBytes;
+  static constexpr int kSmemBytes = 1024 + kBarOffset + 2 * kStages * 8 + 16;
+};
+
+template <int kConsumerWarps, int kStages>
+__global__ void __launch_bounds__(UnitsCfg<kConsumerWarps, kStages>::kThreads, 2)
+    paged_decode_units_kernel(const __grid_constant__ CUtensorMap kv_map, const AttnArgs a) {
+  pdl_wait();
+  pdl_trigger();
+  using Cfg = UnitsCfg<kConsumerWarps, kStages>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* ring = smem;
+  uint8_t* qtile = smem + Cfg::kStageBytes;
+  float* merge = reinterpret_cast<float*>(smem + Cfg::kMergeOff);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::kBarOffset);
+  uint64_t* empty = full + kStages;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kStages);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int n_units = a.n_items * a.num_kv;
+
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  if (warp == kConsumerWarps) {
+    // ---------------- producer warp: every unit's pages, in order, through one ring ----------
+    const uint64_t policy = l2_policy_evict_first();
+    if (lane == 0) tma_prefetch_desc(&kv_map);
+    int g = 0;  // pages issued so far (over all of this CTA's units)
+    bool stop = false;
+    for (int u = blockIdx.x; u < n_units && !stop; u += gridDim.x) {
+      const int item_idx = u / a.num_kv;
+      const int kvh = u - item_idx * a.num_kv;
+      const int* it = a.items + static_cast<long long>(item_idx) * kRec;
+      const int page_begin = it[3], npages = it[4] - it[3];
+      const int* sr = a.seqs + static_cast<long long>(it[0]) * kRec;
+      const int* table = a.tables + sr[4] + page_begin;
+      for (int j0 = 0; j0 < npages && !stop; j0 += 32) {
+        int mine = 0;
+        if (j0 + lane < npages) mine = table[j0 + lane];
+        const int cnt = min(32, npages - j0);
+        for (int jj = 0; jj < cnt; ++jj) {
+          const int blk = __shfl_sync(0xffffffffu, mine, jj);
+          int ok = 1;
+          if (lane == 0) {
+            const int s = g % kStages;
+            if (*abort_flag) ok = 0;
+            if (ok && g >= kStages && !mbar_wait(&empty[s], ((g / kStages) - 1) & 1)) {
+              atomicOr(&g_status_word, kErrTimeout);
+              *abort_flag = 1;
+              ok = 0;
+            }
+            if (ok) {
+              // Out-of-range block ids are flagged; the TMA unit fills such boxes with zeros.
+              if (static_cast<unsigned>(blk) >= static_cast<unsigned>(a.num_blocks))
+                atomicOr(&g_status_word, kErrBlock);
+              mbar_arrive_expect_tx(&full[s], kPageKVBytes);
+              tma_load_5d(ring + s * kPageKVBytes, &kv_map, &full[s], 0, 0, 0, kvh, blk, policy);
+            }
+          }
+          ok = __shfl_sync(0xffffffffu, ok, 0);
+          if (!ok) {
+            stop = true;
+            break;
+          }
+          ++g;
+        }
+      }
+    }
+    // Drain: never leave the CTA with a TMA write in flight.
+    if (lane == 0) {
+      for (int j = g > kStages ? g - kStages : 0; j < g; ++j) {
+        if (!mbar_wait(&full[j % kStages], (j / kStages) & 1)) {
+          atomicOr(&g_status_word, kErrTimeout);
+          break;
+        }
+      }
+    }
+    return;
+  }
+
+  // ---------------- consumer warps ----------------
+  // A unit's 16 query rows (token r / 2, head kvh * 2 + r % 2), 16 chunks of 16 bytes each,
+  // kPer chunks per consumer thread, loaded into registers one unit ahead.
+  constexpr int kPer = 16 * 16 / (kConsumerWarps * 32);
+  static_assert(16 * 16 % (kConsumerWarps * 32) == 0, "query chunks per thread");
+  auto load_q = [&](int u, uint4 (&v)[kPer]) {
+    const int item_idx = u / a.num_kv;
+    const int kvh = u - item_idx * a.num_kv;
+    const int* it = a.items + static_cast<long long>(item_idx) * kRec;
+    const int tok0 = it[1], n_q = it[2];
+    const int flat_start = a.seqs[static_cast<long long>(it[0]) * kRec];
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+      const int c = threadIdx.x + k * kConsumerWarps * 32;
+      const int r = c >> 4;
+      const int d = (c & 15) * 8;
+      const int tok = r >> 1;
+      v[k] = make_uint4(0u, 0u, 0u, 0u);
+      if (tok < n_q)
+        v[k] = __ldg(reinterpret_cast<const uint4*>(
+            a.q + static_cast<long long>(flat_start + tok0 + tok) * a.q_row_stride +
+            (kvh * kGroup + (r & 1)) * kHeadDim + d));
+    }
+  };
+  uint4 qn[kPer];
+  if (blockIdx.x < static_cast<unsigned>(n_units)) load_q(blockIdx.x, qn);
+  const uint32_t ring_u32 = smem_u32(ring);
+  const uint32_t qbase_s = smem_u32(qtile);
+  int g0 = 0;  // this unit's first page in the ring sequence
+  for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
+    const int item_idx = u / a.num_kv;
+    const int kvh = u - item_idx * a.num_kv;
+    const int* it = a.items + static_cast<long long>(item_idx) * kRec;
+    const int seq = it[0], tok0 = it[1], n_q = it[2], page_begin = it[3], page_end = it[4],
+              part_row = it[5];
+    const int merge_row = it[7] == 1 ? it[6] : -1;
+    const int* sr = a.seqs + static_cast<long long>(seq) * kRec;
+    const int flat_start = sr[0], num_cached = sr[2];
+    const int npages = page_end - page_begin;
+
+    // The previous unit's merge has finished with the query tile and the merge scratch.
+    asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+      const int c = threadIdx.x + k * kConsumerWarps * 32;
+      const int r = c >> 4;
+      const int d = (c & 15) * 8;
+      asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(
+                       qbase_s + (r >> 4) * (16 * kHeadDim * 2) + swz_off(r & 15, d, 16)),
+                   "r"(qn[k].x), "r"(qn[k].y), "r"(qn[k].z), "r"(qn[k].w)
+                   : "memory");
+    }
+    asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
+    uint32_t qf[8][4];
+    {
+      const int mi = lane >> 3;
+      const int row = (lane & 7) + (mi & 1) * 8;
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks)
+        ldsm_x4(qbase_s + swz_off(row, ks * 16 + (mi >> 1) * 8, 16), qf[ks][0], qf[ks][1],
+                qf[ks][2], qf[ks][3]);
+    }
+    if (u + static_cast<int>(gridDim.x) < n_units) load_q(u + gridDim.x, qn);
+
+    float o[16][4];
+#pragma unroll
+    for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+    float m[2] = {-INFINITY, -INFINITY};
+    float l[2] = {0.f, 0.f};
+    const int r0 = lane >> 2;
+    const int r1 = r0 + 8;
+    const int qpos_base = num_cached + tok0;
+    const int qpos0 = qpos_base + (r0 >> 1);
+    const int qpos1 = qpos_base + (r1 >> 1);
+    const int min_qpos = qpos_base;
+    const int max_qpos = qpos_base + 7;
+    for (int j = warp; j < npages; j += kConsumerWarps) {
+      const int gj = g0 + j;
+      const int s = gj % kStages;
+      // Leave the loop only as a whole warp: the tensor-core ops below are warp-collective.
+      const bool ok =
+          __all_sync(0xffffffffu, mbar_wait_fast(&full[s], (gj / kStages) & 1, abort_flag));
+      if (!ok) {
+        if (lane == 0) {
+          atomicOr(&g_status_word, kErrTimeout);
+          *abort_flag = 1;
+        }
+        break;
+      }
+      const int key0 = (page_begin + j) * kBlockTokens;
+      if (key0 <= max_qpos) {
+        attend_page(ring_u32 + s * kPageKVBytes, qf, o, m, l, key0, qpos0, qpos1,
+                    key0 + kBlockTokens - 1 > min_qpos, a.scale_log2, lane);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      l[i] += __shfl_xor_sync(0xffffffffu, l[i], 1);
+      l[i] += __shfl_xor_sync(0xffffffffu, l[i], 2);
+    }
+    decode_merge_store<kConsumerWarps>(merge, o, m, l, warp, lane, n_q, kvh, part_row, merge_row,
+                                       flat_start, tok0, a);
+    g0 += npages;
   }
 }
 

@@ -22,6 +22,7 @@
 //     whose epilogue merges the prefix partials.
 // Items are ordered longest first so the hardware block scheduler fills the tail with short ones.
 #include <algorithm>
+#include <climits>
 #include <cstdint>
 #include <cstring>
 #include <string>
@@ -415,6 +416,9 @@ extern "C" int ms_plan_build(int32_t num_seqs, const int32_t* flat_start, const 
   info->off_tile = static_cast<int32_t>(off_tile);
   info->n_tc_items = static_cast<int32_t>(tcv.size());
   info->n_cascade = static_cast<int32_t>(groups.size());
+  int64_t decode_pages = 0;
+  for (const Item& t : dec) decode_pages += t.pe - t.pb;
+  info->decode_pages = static_cast<int32_t>(std::min<int64_t>(decode_pages, INT32_MAX));
   info->off_tc = static_cast<int32_t>(off_tc);
   info->off_combine = static_cast<int32_t>(off_combine);
   info->total_ints = static_cast<int32_t>(total);

@@ -135,6 +135,19 @@ def test_config5_contexts_on_a_non_aliased_subset(cuda_device: torch.device) -> 
         assert err <= ATOL, (split, err)
 
 
+@pytest.mark.parametrize("pages_per_split", [0, 8])
+def test_many_short_decode_rows(pages_per_split: int, cuda_device: torch.device) -> None:
+    """80 decode and verify rows over 10-400 cached tokens: more decode CTAs than one resident
+    wave and few pages each, which the persistent decode kernel serves (with forced splits, its
+    partial-row path and the combine too).  Against the fp32 oracle."""
+    import numpy as np
+
+    rng = np.random.default_rng(31)
+    rows = [(int(rng.choice([1, 1, 1, 5])), int(rng.integers(10, 400))) for _ in range(80)]
+    err = _random_case_vs_fp32(custom(rows, seed=31), 31, pages_per_split, cuda_device)
+    assert err <= ATOL, err
+
+
 @pytest.mark.parametrize("num_seqs", [16, 64, 512], ids=["16_rows", "64_rows", "config4"])
 def test_cascade_shared_prefix(num_seqs: int, cuda_device: torch.device) -> None:
     """Config 4's geometry (5-token verify rows sharing a 1024-token prefix, 64..256 own tokens):
