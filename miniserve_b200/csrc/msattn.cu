@@ -189,6 +189,9 @@ static int ensure_smem_attrs() {
   e = cudaFuncSetAttribute(ms::paged_decode_units_kernel<kDecodeWarps, kDecodeStages>,
                            cudaFuncAttributeMaxDynamicSharedMemorySize, UnitsCfg::kSmemBytes);
   if (e != cudaSuccess) return cuda_fail("cudaFuncSetAttribute(decode units)", e);
+  e = cudaFuncSetAttribute(ms::paged_decode_units_kernel<kDecodeWarps, kDecodeStages, true>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, UnitsCfg::kSmemBytes);
+  if (e != cudaSuccess) return cuda_fail("cudaFuncSetAttribute(decode units, cascade)", e);
   e = cudaFuncSetAttribute(ms::paged_attn_kernel<1, kTileWarps, kTileStages, true>,
                            cudaFuncAttributeMaxDynamicSharedMemorySize, TileCfg::kSmemBytes);
   if (e != cudaSuccess) return cuda_fail("cudaFuncSetAttribute(tile, early)", e);
@@ -641,9 +644,14 @@ extern "C" int ms_paged_attention(const void* q, int64_t q_row_stride, void* out
                  DecodeCfg::kThreads, DecodeCfg::kSmemBytes, ds, map, a);
     } else if (static_cast<int64_t>(plan->decode_pages) <=
                static_cast<int64_t>(kUnitsMaxAvgPages) * plan->n_decode_items) {
-      // Many short items: two persistent CTAs per SM walk the work units.
-      e = launch(ms::paged_decode_units_kernel<kDecodeWarps, kDecodeStages>, 2 * sms,
-                 UnitsCfg::kThreads, UnitsCfg::kSmemBytes, ds, map, a);
+      // Many short items: two persistent CTAs per SM walk the work units.  Right after the
+      // tensor-core kernel of a cascade plan they also overlap its last wave.
+      const bool after_prefix = plan->n_cascade > 0 && plan->n_tc_items > 0 && ds == s;
+      e = after_prefix
+              ? launch(ms::paged_decode_units_kernel<kDecodeWarps, kDecodeStages, true>, 2 * sms,
+                       UnitsCfg::kThreads, UnitsCfg::kSmemBytes, ds, map, a)
+              : launch(ms::paged_decode_units_kernel<kDecodeWarps, kDecodeStages>, 2 * sms,
+                       UnitsCfg::kThreads, UnitsCfg::kSmemBytes, ds, map, a);
     } else {
       e = launch(ms::paged_attn_kernel<0, kDecodeWarps, kDecodeStages>, ctas,
                  DecodeCfg::kThreads, DecodeCfg::kSmemBytes, ds, map, a);

@@ -157,7 +157,7 @@ __device__ unsigned g_status_word;  // device status bits (kErr*), read by ms_de
 // sums) and write the rows: bf16 output (merged with a cascade row's shared-prefix partial when
 // merge_row >= 0) or fp32 partial rows and log2-sum-exp for split items.  Called by every
 // consumer thread (threadIdx.x < 32 * kConsumerWarps); uses named barrier 1.
-template <int kConsumerWarps>
+template <int kConsumerWarps, bool kWaitBeforeMerge = false>
 __device__ __forceinline__ void decode_merge_store(float* merge, const float (&o)[16][4],
                                                    const float (&m)[2], const float (&l)[2],
                                                    int warp, int lane, int n_q, int kvh,
@@ -220,6 +220,7 @@ __device__ __forceinline__ void decode_merge_store(float* merge, const float (&o
       if (merge_row >= 0) {
         // Cascade row: merge the shared-prefix partial (normalised O and log2-sum-exp) that the
         // tensor-core kernel wrote before this launch: out = (acc 2^(mx-M) + O_p L_p') / (...).
+        if constexpr (kWaitBeforeMerge) pdl_wait();  // the partial is that kernel's output
         const long long prow = static_cast<long long>(merge_row + r) * a.num_kv + kvh;
         const float lse_p = a.ws_lse[prow];
         const float lse_u = L > 0.f ? mx + __log2f(L) : -INFINITY;
@@ -516,10 +517,17 @@ struct UnitsCfg {
   static constexpr int kSmemBytes = 1024 + kBarOffset + 2 * kStages * 8 + 16;
 };
 
-template <int kConsumerWarps, int kStages>
+// kAfterPrefix: this launch directly follows the tensor-core kernel of a plan with cascade groups
+// (launched with programmatic dependent launch).  That kernel triggers its dependents only after
+// its own wait has returned, so when this grid starts the kernel before it (which wrote the
+// queries and this step's K/V rows) has completed: everything except the shared-prefix partials
+// may be read at once, and the page loops run during the tensor-core kernel's last wave.  The
+// prefix partials are read after pdl_wait(), and every thread waits before it exits, so this
+// grid never completes before the tensor-core kernel (later kernels rely on that ordering).
+template <int kConsumerWarps, int kStages, bool kAfterPrefix = false>
 __global__ void __launch_bounds__(UnitsCfg<kConsumerWarps, kStages>::kThreads, 2)
     paged_decode_units_kernel(const __grid_constant__ CUtensorMap kv_map, const AttnArgs a) {
-  pdl_wait();
+  if constexpr (!kAfterPrefix) pdl_wait();
   pdl_trigger();
   using Cfg = UnitsCfg<kConsumerWarps, kStages>;
   extern __shared__ uint8_t smem_raw[];
@@ -601,6 +609,7 @@ __global__ void __launch_bounds__(UnitsCfg<kConsumerWarps, kStages>::kThreads, 2
         }
       }
     }
+    if constexpr (kAfterPrefix) pdl_wait();
     return;
   }
 
@@ -706,10 +715,11 @@ __global__ void __launch_bounds__(UnitsCfg<kConsumerWarps, kStages>::kThreads, 2
       l[i] += __shfl_xor_sync(0xffffffffu, l[i], 1);
       l[i] += __shfl_xor_sync(0xffffffffu, l[i], 2);
     }
-    decode_merge_store<kConsumerWarps>(merge, o, m, l, warp, lane, n_q, kvh, part_row, merge_row,
-                                       flat_start, tok0, a);
+    decode_merge_store<kConsumerWarps, kAfterPrefix>(merge, o, m, l, warp, lane, n_q, kvh,
+                                                     part_row, merge_row, flat_start, tok0, a);
     g0 += npages;
   }
+  if constexpr (kAfterPrefix) pdl_wait();
 }
 
 struct CombineArgs {

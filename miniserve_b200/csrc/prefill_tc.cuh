@@ -163,6 +163,8 @@ __device__ __forceinline__ void exp_pack32(const float (&sv)[32], float2 sc2, fl
 __global__ void __launch_bounds__(TcCfg::kThreads, 1)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap k_map,
                       const __grid_constant__ CUtensorMap v_map, const AttnArgs a) {
+  // The trigger comes after the wait: a grid launched behind this one then knows that the kernel
+  // before this one has completed (the persistent decode kernel relies on it for cascade plans).
   pdl_wait();
   pdl_trigger();
   extern __shared__ uint8_t smem_raw[];
