@@ -144,6 +144,8 @@ def check_plan(chunks: list[SeqChunk], num_tokens: int, split: int = 0) -> None:
         if c.num_new <= 64 and c_idx not in cascade:
             assert (c_idx, 0) in cover
     assert info.workspace_bytes_per_kv_head == info.part_rows * 129 * 4
+    # decode_pages: the pages the decode / verify items read (it picks the decode kernel form)
+    assert info.decode_pages == int(sum(int(it[4] - it[3]) for it in dec))
 
 
 @pytest.mark.parametrize("make", [config1, config2, config3, config4])
