@@ -19,6 +19,11 @@ from . import _capi
 from .attention import AttentionMetadata, _rows, _stream, attend
 from .kv_pool import HEAD_DIM, check_layer_views
 
+# Smallest step (tokens) for which ``fused_qkv="auto"`` takes kernel E: measured on a B200 against
+# cuBLAS + kernel A over 28 layers, kernel E is 0.82-0.96x from 256 to 768 tokens and 1.05-1.44x
+# from 1024 tokens up.
+FUSED_QKV_MIN_TOKENS = 1024
+
 
 class HeadNorm(nn.Module):
     """Holds an RMSNorm's weight and eps (layers.py:10-22); applied inside kernel A."""
@@ -150,9 +155,13 @@ class Qwen3Attention(nn.Module):
         self.q_norm = HeadNorm(self.head_dim, cfg.rms_norm_eps)
         self.k_norm = HeadNorm(self.head_dim, cfg.rms_norm_eps)
         # True: kernel E computes the projection and the norm/RoPE/scatter in one launch (faster
-        # from a few thousand tokens per step; a projection output can differ from cuBLAS's by one
-        # bf16 ulp, from the GEMM's accumulation order).  False: cuBLAS, then kernel A.
-        self.fused_qkv = bool(getattr(cfg, "fused_qkv", False))
+        # from about a thousand tokens per step; a projection output can differ from cuBLAS's by
+        # one bf16 ulp, from the GEMM's accumulation order).  False: cuBLAS, then kernel A.
+        # "auto": kernel E for steps of at least FUSED_QKV_MIN_TOKENS tokens, else cuBLAS + A.
+        fused = getattr(cfg, "fused_qkv", False)
+        if fused != "auto" and not isinstance(fused, (bool, int)):
+            raise ValueError(f"fused_qkv must be True, False or 'auto', not {fused!r}")
+        self.fused_qkv: bool | str = fused if fused == "auto" else bool(fused)
 
     def forward(
         self,
@@ -164,7 +173,8 @@ class Qwen3Attention(nn.Module):
         meta: AttentionMetadata,
     ) -> Tensor:
         t = x.shape[0]
-        if self.fused_qkv and isinstance(self.qkv_proj, nn.Linear):
+        fused = self.fused_qkv is True or (self.fused_qkv == "auto" and t >= FUSED_QKV_MIN_TOKENS)
+        if fused and isinstance(self.qkv_proj, nn.Linear):
             q = qkv_proj_norm_rope_scatter(
                 x, self.qkv_proj.weight, self.q_norm.weight, self.k_norm.weight, self.q_norm.eps,
                 cos, sin, meta.slot_mapping, k_cache, v_cache, self.num_heads,
