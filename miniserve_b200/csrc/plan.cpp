@@ -242,8 +242,29 @@ extern "C" int ms_plan_build(int32_t num_seqs, const int32_t* flat_start, const 
   } else if (n_tc_tiles * kTcAssumedKvHeads >= num_sms) {
     tc_split64 = int64_t(1) << 30;
   } else {
+    // The smallest split (whole 128-key blocks, at least kTcAutoMinSplitPages) whose items fit
+    // one wave, one CTA per SM.  The work-per-CTA estimate alone is not enough: every tile's
+    // split count rounds up, which can leave a thin second wave (8 tiles over 8192 cached tokens:
+    // 240 pages gave 24 items, 192 CTAs).  The CTA count does not grow with the split, so the
+    // split is found by bisection; at the longest tile's page count every tile is one item and
+    // the items fit (this branch has fewer tiles x heads than SMs).
+    auto tc_ctas_at = [&](int64_t p) {
+      int64_t items = 0;
+      for (const Item& t : tiles)
+        if (num_new[t.seq] > kTileTokens && cascade_pages[t.seq] == 0) items += (t.pe + p - 1) / p;
+      return items * kTcAssumedKvHeads;
+    };
+    int64_t max_pe = 0;
+    for (const Item& t : tiles)
+      if (num_new[t.seq] > kTileTokens) max_pe = std::max<int64_t>(max_pe, t.pe);
     const int64_t per_cta = (tc_pages * kTcAssumedKvHeads + num_sms - 1) / std::max(num_sms, 1);
-    tc_split64 = std::max<int64_t>(kTcAutoMinSplitPages, round_blocks(per_cta));
+    int64_t lo = std::max<int64_t>(kTcAutoMinSplitPages, round_blocks(per_cta)) / kTcBlockPages;
+    int64_t hi = std::max<int64_t>(lo, round_blocks(max_pe) / kTcBlockPages);
+    while (lo < hi) {
+      const int64_t mid = (lo + hi) / 2;
+      if (tc_ctas_at(mid * kTcBlockPages) <= num_sms) hi = mid; else lo = mid + 1;
+    }
+    tc_split64 = lo * kTcBlockPages;
   }
   const int tc_split = static_cast<int>(std::min<int64_t>(tc_split64, int64_t(1) << 30));
   const bool tc_zigzag = pages_per_split > 0 || n_tc_tiles * kTcAssumedKvHeads < num_sms;

@@ -167,6 +167,24 @@ def test_plan_random_ragged_batches(seed: int) -> None:
     check_plan(b.chunks, b.num_tokens, int(rng.integers(0, 20)))
 
 
+@pytest.mark.parametrize("rows", [
+    [(1024, 8192)], [(512, 8192)], [(2048, 16384)], [(1024, 4096)], [(768, 12000)],
+    [(1024, 8192), (1024, 8192)], [(128, 32768)], [(300, 20000), (90, 5000)],
+])
+def test_tc_split_fits_one_wave(rows) -> None:
+    """Prefill chunks over long caches, with fewer tensor-core tiles x KV heads than SMs, are
+    split into more items but never beyond one wave of CTAs (one per SM); split ranges start on
+    whole 128-key blocks, and the plan stays a complete cover."""
+    b = custom(rows, seed=2)
+    check_plan(b.chunks, b.num_tokens)
+    packed, info = plan_batch(b.chunks, b.num_tokens, 16, 148, 0)
+    tiles = sum((c.num_new + 127) // 128 for c in b.chunks)
+    assert tiles * 8 < 148
+    assert tiles < info.n_tc_items and info.n_tc_items * 8 <= 148
+    _, _, _, tcv, _ = decode_plan(packed, info)
+    assert all(int(it[3]) % 8 == 0 for it in tcv)
+
+
 def test_empty_batch() -> None:
     packed, info = plan_batch([], 0)
     assert info.n_decode_items == info.n_tile_items == info.n_combine == 0
