@@ -89,7 +89,8 @@ typedef struct MsPlanInfo {
                               their own pages; sequence records num_seqs .. num_seqs+n_cascade-1
                               describe the groups */
   int32_t decode_pages;    /* pages (per KV head) the decode / verify items read, in total */
-  int32_t reserved[4];
+  int32_t combine_tokens_max; /* most query tokens of one combine record (sizes its grid) */
+  int32_t reserved[3];
 } MsPlanInfo;
 
 /* Upper bound on the packed buffer length (int32 elements) for a batch of this size. */

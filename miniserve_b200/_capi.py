@@ -62,7 +62,8 @@ class MsPlanInfo(C.Structure):
         ("off_tc", C.c_int32),
         ("n_cascade", C.c_int32),
         ("decode_pages", C.c_int32),
-        ("reserved", C.c_int32 * 4),
+        ("combine_tokens_max", C.c_int32),
+        ("reserved", C.c_int32 * 3),
     ]
 
 

@@ -140,10 +140,10 @@ static int matrix_tile_map(const void* base, int64_t rows, int64_t cols, int64_t
 // Every kernel is launched with programmatic stream serialization (see pdl_wait in
 // ms_common.cuh): its grid may start while the previous kernel in the stream finishes.
 template <typename... KArgs, typename... Args>
-static cudaError_t launch(void (*kernel)(KArgs...), unsigned grid, unsigned block, size_t smem,
+static cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, unsigned block, size_t smem,
                           cudaStream_t stream, Args&&... args) {
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grid);
+  cfg.gridDim = grid;
   cfg.blockDim = dim3(block);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
@@ -689,8 +689,13 @@ extern "C" int ms_paged_attention(const void* q, int64_t q_row_stride, void* out
     c.num_kv = num_kv_heads;
     c.ws_o = a.ws_o;
     c.ws_lse = a.ws_lse;
-    const cudaError_t e =
-        launch(ms::combine_kernel, plan->n_combine * num_kv_heads, ms::kCombineThreads, 0, s, c);
+    // One CTA per (record, KV head, kCombineRows rows): a tensor-core record has 256 rows, and
+    // one CTA walking them all is latency-bound (each row is a few dependent loads).
+    const int64_t rows_max = static_cast<int64_t>(std::max(plan->combine_tokens_max, 1)) * 2;
+    const unsigned row_ctas = static_cast<unsigned>(
+        std::min<int64_t>((rows_max + ms::kCombineRows - 1) / ms::kCombineRows, 65535));
+    const cudaError_t e = launch(ms::combine_kernel, dim3(plan->n_combine * num_kv_heads, row_ctas),
+                                 ms::kCombineThreads, 0, s, c);
     if (e != cudaSuccess) return cuda_fail("combine launch", e);
   }
   return MS_OK;

@@ -734,8 +734,9 @@ struct CombineArgs {
 };
 
 // Kernel C: out = sum_s 2^(lse_s - M) * O_s / sum_s 2^(lse_s - M) for every split tile.
-// One CTA per (split tile, KV head); thread = (row, 16-dim slice), 32 rows per pass.
+// One CTA per (split tile, KV head, run of kCombineRows rows); thread = (row, 16-dim slice).
 constexpr int kCombineThreads = 256;
+constexpr int kCombineRows = kCombineThreads / 8;  // rows one CTA merges at a time (8 threads each)
 __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const CombineArgs a) {
   pdl_wait();
   pdl_trigger();
@@ -749,7 +750,9 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const CombineA
   // a cascade row's shared-prefix and own-page partials sit apart (stride in field 5).
   const int stride = cr[5] != 0 ? cr[5] : rows;
   const int dc = (threadIdx.x & 7) * 16;
-  for (int r = threadIdx.x >> 3; r < rows; r += kCombineThreads / 8) {
+  // Grid y splits the record's rows into runs of kCombineRows; CTAs past its rows do nothing.
+  for (int r = blockIdx.y * kCombineRows + (threadIdx.x >> 3); r < rows;
+       r += gridDim.y * kCombineRows) {
     float mx = -INFINITY;
     for (int s = 0; s < n_splits; ++s)
       mx = fmaxf(mx, a.ws_lse[(static_cast<long long>(part_row0) + static_cast<long long>(s) * stride + r) *

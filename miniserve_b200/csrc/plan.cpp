@@ -440,6 +440,9 @@ extern "C" int ms_plan_build(int32_t num_seqs, const int32_t* flat_start, const 
   int64_t decode_pages = 0;
   for (const Item& t : dec) decode_pages += t.pe - t.pb;
   info->decode_pages = static_cast<int32_t>(std::min<int64_t>(decode_pages, INT32_MAX));
+  int combine_tokens_max = 0;
+  for (const Item& c : comb) combine_tokens_max = std::max(combine_tokens_max, c.n_q);
+  info->combine_tokens_max = combine_tokens_max;
   info->off_tc = static_cast<int32_t>(off_tc);
   info->off_combine = static_cast<int32_t>(off_combine);
   info->total_ints = static_cast<int32_t>(total);

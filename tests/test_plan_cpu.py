@@ -146,6 +146,8 @@ def check_plan(chunks: list[SeqChunk], num_tokens: int, split: int = 0) -> None:
     assert info.workspace_bytes_per_kv_head == info.part_rows * 129 * 4
     # decode_pages: the pages the decode / verify items read (it picks the decode kernel form)
     assert info.decode_pages == int(sum(int(it[4] - it[3]) for it in dec))
+    # combine_tokens_max: the most query tokens of one combine record (it sizes the combine grid)
+    assert info.combine_tokens_max == max((int(c[2]) for c in comb), default=0)
 
 
 @pytest.mark.parametrize("make", [config1, config2, config3, config4])
