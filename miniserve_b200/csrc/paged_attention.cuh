@@ -13,8 +13,12 @@
 //     accumulate) and an fp32 online softmax in the exp2 domain.
 //   * Decode mode (<= 8 query tokens, 16 rows): each consumer warp takes every 4th page and the
 //     warps merge their (m, l, O) in shared memory at the end.
-//   * Tile mode (up to 64 query tokens, 128 rows): each consumer warp owns 16 rows and reads
-//     every page; causal masking uses the sequence's cached length as the offset.
+//   * Tile mode (up to 64 query tokens, 128 rows): each consumer warp owns 16 rows; causal
+//     masking uses the sequence's cached length as the offset.  A tile of at most 32 tokens
+//     (R <= 4 row groups of 16) leaves warps without rows, so the 8 warps form P = 4 (R <= 2) or
+//     P = 2 (R <= 4) page phases of 8 / P warps each: warp w takes row group w % (8 / P) and the
+//     pages j with j % P == w / (8 / P), and the phases merge their (m, l, O) through the idle
+//     ring at the end.  Longer tiles keep one phase: every warp reads every page.
 //   * An item that covers the whole visible context writes bf16 output rows directly; a split
 //     item writes normalised fp32 partials + log2-sum-exp, merged by kernel C.
 //
@@ -54,7 +58,10 @@ struct AttnCfg {
   static constexpr int kThreads = (kConsumerWarps + 1) * 32;
   static constexpr int kStageBytes = kStages * kPageKVBytes;
   static constexpr int kQBytes = kRows * kHeadDim * 2;
-  static constexpr int kMergeBytes = kMode == 0 ? kConsumerWarps * 16 * (kHeadDim + 4) * 4 + 2 * kConsumerWarps * 16 * 4 : 0;
+  // Decode mode: every warp's 16 rows of (O, m, l).  Tile mode: the lane-ordered (O, m, l) of the
+  // warps outside page phase 0 (at most 6 of 8).
+  static constexpr int kMergeBytes = kMode == 0 ? kConsumerWarps * 16 * (kHeadDim + 4) * 4 + 2 * kConsumerWarps * 16 * 4
+                                                : (kConsumerWarps - kConsumerWarps / 4) * 17 * 32 * 16;
   static_assert(kMergeBytes <= kStageBytes, "merge scratch reuses the stage ring");
   static constexpr int kBarOffset = kStageBytes + kQBytes;
   static constexpr int kSmemBytes = 1024 + kBarOffset + 2 * kStages * 8 + 16;
@@ -295,6 +302,12 @@ __global__ void __launch_bounds__(AttnCfg<kMode, kConsumerWarps, kStages>::kThre
   // Decode items of cascade rows (field 7 = 1) merge the shared-prefix partial rows starting at
   // field 6 into their output.
   const int merge_row = (kMode == 0 && it[7] == 1) ? it[6] : -1;
+  // Tile mode: page phases (see the top of this file); decode mode splits pages by warp.
+  static_assert(kMode == 0 || (kConsumerWarps == 8 && kStages % 4 == 0),
+                "tile-mode page phases need 8 consumer warps and a ring of a multiple of 4 stages");
+  const int row_groups = (2 * n_q + 15) >> 4;
+  const int phases = kMode == 0 ? 1 : (row_groups <= 2 ? 4 : (row_groups <= 4 ? 2 : 1));
+  const int phase_warps = kConsumerWarps / phases;  // warps per phase (tile mode)
   const int* sr = a.seqs + static_cast<long long>(seq) * kRec;
   const int flat_start = sr[0], num_cached = sr[2], table_off = sr[4];
   const int npages = page_end - page_begin;
@@ -303,7 +316,7 @@ __global__ void __launch_bounds__(AttnCfg<kMode, kConsumerWarps, kStages>::kThre
 #pragma unroll
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kMode == 0 ? 1 : kConsumerWarps);
+      mbar_init(&empty[s], kMode == 0 ? 1 : phase_warps);  // the warps that read the page
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -408,7 +421,7 @@ __global__ void __launch_bounds__(AttnCfg<kMode, kConsumerWarps, kStages>::kThre
   }
 
   // ---------------- consumer warps ----------------
-  const int row_base = kMode == 0 ? 0 : warp * 16;
+  const int row_base = kMode == 0 ? 0 : (warp % phase_warps) * 16;
   uint32_t qf[8][4];
   {
     const uint32_t qbase = smem_u32(qtile) + (row_base >> 4) * (16 * kHeadDim * 2);
@@ -433,8 +446,8 @@ __global__ void __launch_bounds__(AttnCfg<kMode, kConsumerWarps, kStages>::kThre
   const int max_qpos = qpos_base + ((row_base + 15) >> 1);  // last row (warp-uniform)
   const uint32_t ring_u32 = smem_u32(ring);
 
-  const int jstart = kMode == 0 ? warp : 0;
-  const int jstep = kMode == 0 ? kConsumerWarps : 1;
+  const int jstart = kMode == 0 ? warp : warp / phase_warps;
+  const int jstep = kMode == 0 ? kConsumerWarps : phases;
   const bool warp_active = kMode == 0 || (row_base >> 1) < n_q;
   for (int j = jstart; j < npages; j += jstep) {
     const int s = j % kStages;
@@ -468,7 +481,46 @@ __global__ void __launch_bounds__(AttnCfg<kMode, kConsumerWarps, kStages>::kThre
     decode_merge_store<kConsumerWarps>(reinterpret_cast<float*>(ring), o, m, l, warp, lane, n_q,
                                        kvh, part_row, merge_row, flat_start, tok0, a);
   } else {
-    if (!warp_active) return;
+    if (phases > 1) {
+      // Merge the page phases of each row group into phase 0's warp, lane by lane (the warps of
+      // one row group hold the same rows and columns in the same lanes), through the ring: every
+      // page has been consumed once all consumer warps reach the barrier.
+      float4* scratch = reinterpret_cast<float4*>(ring);
+      const int slot = warp - phase_warps;  // warps of phases 1.. in order
+      asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
+      if (slot >= 0 && warp_active) {
+#pragma unroll
+        for (int n = 0; n < 16; ++n)
+          scratch[(slot * 17 + n) * 32 + lane] = make_float4(o[n][0], o[n][1], o[n][2], o[n][3]);
+        scratch[(slot * 17 + 16) * 32 + lane] = make_float4(m[0], m[1], l[0], l[1]);
+      }
+      asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
+      if (slot >= 0 || !warp_active) return;
+      for (int p = 1; p < phases; ++p) {
+        const int sl = (p - 1) * phase_warps + warp;
+        const float4 ml = scratch[(sl * 17 + 16) * 32 + lane];
+        const float mp[2] = {ml.x, ml.y}, lp[2] = {ml.z, ml.w};
+        float wa[2], wb[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const float mx = fmaxf(m[h], mp[h]);
+          wa[h] = m[h] == -INFINITY ? 0.f : fast_exp2(m[h] - mx);
+          wb[h] = mp[h] == -INFINITY ? 0.f : fast_exp2(mp[h] - mx);
+          l[h] = l[h] * wa[h] + lp[h] * wb[h];
+          m[h] = mx;
+        }
+#pragma unroll
+        for (int n = 0; n < 16; ++n) {
+          const float4 v = scratch[(sl * 17 + n) * 32 + lane];
+          o[n][0] = o[n][0] * wa[0] + v.x * wb[0];
+          o[n][1] = o[n][1] * wa[0] + v.y * wb[0];
+          o[n][2] = o[n][2] * wa[1] + v.z * wb[1];
+          o[n][3] = o[n][3] * wa[1] + v.w * wb[1];
+        }
+      }
+    } else if (!warp_active) {
+      return;
+    }
     const int c = 2 * (lane & 3);
 #pragma unroll
     for (int half = 0; half < 2; ++half) {

@@ -119,6 +119,19 @@ def test_tensor_core_prefill_edges(rows, cuda_device: torch.device) -> None:
         assert err <= ATOL, (split, err)
 
 
+@pytest.mark.parametrize("rows", [
+    [(9, 700), (16, 1500), (12, 40)], [(17, 300), (24, 2000), (32, 90)], [(33, 100), (64, 900)],
+    [(16, 0), (32, 0), (9, 16)], [(10, 3000)] * 12,
+], ids=["4_phases", "2_phases", "1_phase", "fresh", "many_4_phase"])
+def test_tile_mode_page_phases(rows, cuda_device: torch.device) -> None:
+    """Kernel B's tile mode (9-64-token chunks): tiles of <= 16 tokens split their pages over 4
+    phases of warps, <= 32 tokens over 2, longer ones over 1; the phases merge at the end.  Whole
+    and split items (whose partials the combine pass merges), against the fp32 oracle."""
+    for split in (0, 8, 64):
+        err = _random_case_vs_fp32(custom(rows, seed=len(rows) + 40), 5, split, cuda_device)
+        assert err <= ATOL, (split, err)
+
+
 def test_config5_contexts_on_a_non_aliased_subset(cuda_device: torch.device) -> None:
     """Config 5's heavy-tailed contexts (logU[512, 32768]): its shortest, longest and quantile
     rows, each with its own blocks (no pool aliasing), against the fp32 oracle; automatic and
