@@ -45,9 +45,12 @@ constexpr int kTcTokens = 128;       // query tokens per tensor-core work item (
 // kTcAssumedKvHeads CTAs per item -- or no split (up to kMaxSplitPages) when the rows alone
 // exceed a wave.  Measured on 1x B200 (us per attention call): 1 row of 32K tokens 36.4 with
 // 64-page splits vs 50.2 with 32; 4 x 16K 47.6 (128) vs 64.5 (32); config 3's 48 decode rows
-// 41.0 unsplit vs 46.5 (32).  Splits that leave a thin second wave are the worst case.
+// 41.0 unsplit vs 46.5 (32).  Splits that leave a thin second wave are the worst case.  Small
+// batches far below a wave split down to 8 pages: 8 rows of U[1, 512] context 12.5 -> 9.9 us per
+// layer-step (one page range per CTA streams at only a few tens of GB/s); 16 rows of 1000
+// tokens 20.8 -> 14.7 us; 8 verify rows of 5 over 2000 22.9 -> 16.4 us.
 constexpr int kDecodeCtasPerSm = 2;
-constexpr int kMinSplitPages = 64;
+constexpr int kMinSplitPages = 8;
 constexpr int kMaxSplitPages = 512;
 constexpr int kTcBlockPages = 8;     // 128-key blocks of the tensor-core kernel
 constexpr int kTcMinSplitPages = 32; // forced splits: tensor-core items cover at least 4 blocks
