@@ -53,6 +53,30 @@ def test_abi_struct_size_matches_header() -> None:
     assert ctypes.sizeof(_capi.MsPlanInfo) == 104
 
 
+def test_abi_struct_layout_matches_header(tmp_path: Path) -> None:
+    """Every MsPlanInfo field sits at the same offset (and the struct has the same size) in the
+    C header as in the ctypes binding: a C program compiled against the header prints them."""
+    import shutil
+    import subprocess
+
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    names = [name for name, _ in _capi.MsPlanInfo._fields_]
+    src = ["#include <stddef.h>", "#include <stdio.h>", f'#include "{HEADER}"', "int main(void) {",
+           '  printf("size %zu\\n", sizeof(MsPlanInfo));']
+    src += [f'  printf("{n} %zu\\n", offsetof(MsPlanInfo, {n}));' for n in names]
+    src += ["  return 0;", "}"]
+    (tmp_path / "layout.c").write_text("\n".join(src) + "\n")
+    exe = tmp_path / "layout"
+    subprocess.run([cc, "-std=c11", "-o", str(exe), str(tmp_path / "layout.c")], check=True)
+    got = dict(line.split() for line in subprocess.run([str(exe)], capture_output=True, text=True,
+                                                       check=True).stdout.splitlines())
+    assert int(got.pop("size")) == ctypes.sizeof(_capi.MsPlanInfo)
+    for n in names:
+        assert int(got[n]) == getattr(_capi.MsPlanInfo, n).offset, n
+
+
 def test_calls_reject_bad_arguments_without_touching_a_gpu(lib: ctypes.CDLL) -> None:
     # Argument validation happens before any CUDA call.
     rc = lib.ms_paged_attention(None, 0, None, 0, 16, 8, None, None, 0, None, None, None, 0,
