@@ -218,8 +218,24 @@ extern "C" int ms_plan_build(int32_t num_seqs, const int32_t* flat_start, const 
     // items_at() does not grow with the split, so the smallest fitting split is found by
     // bisection over multiples of 8 pages.
     int lo = kMinSplitPages / 8, hi = kMaxSplitPages / 8;
+    bool has_tc = !groups.empty();
+    for (const Item& t : tiles) has_tc = has_tc || num_new[t.seq] > kTileTokens;
     if (items_at(hi * 8) > target_items) {
+      // The rows alone exceed a wave.  Longest-first order then packs the waves, except that an
+      // item longer than the pages per item-slot (all pages / a wave's items) outlasts them:
+      // without tensor-core work, split just those, into pieces of about that size (60 rows of
+      // 100 tokens + 4 of 4000: 77.0 -> 25.2 us).  Beside tensor-core work the decode launch
+      // overlaps it on a second stream and a combine pass would wait for both: config 3 measured
+      // 77.4 -> 84.6 us per layer-step with such splits, so they stay whole there.
       split = kMaxSplitPages;
+      if (!has_tc) {
+        int64_t pages = 0;
+        for (const Item& t : tiles)
+          if (num_new[t.seq] <= kTileTokens && cascade_pages[t.seq] == 0) pages += t.pe;
+        const int64_t per_slot = (pages + target_items - 1) / target_items;
+        split = static_cast<int>(std::min<int64_t>(
+            kMaxSplitPages, std::max<int64_t>(kMinSplitPages, (per_slot + 7) / 8 * 8)));
+      }
     } else {
       while (lo < hi) {
         const int mid = (lo + hi) / 2;

@@ -132,6 +132,14 @@ def test_tile_mode_page_phases(rows, cuda_device: torch.device) -> None:
         assert err <= ATOL, (split, err)
 
 
+def test_decode_outlier_rows_split(cuda_device: torch.device) -> None:
+    """60 short decode rows and 4 long ones: the long rows are split (plan without tensor-core
+    work) and merged by the combine pass; against the fp32 oracle."""
+    rows = [(1, 100)] * 60 + [(1, 4000)] * 4
+    err = _random_case_vs_fp32(custom(rows, seed=44), 44, 0, cuda_device)
+    assert err <= ATOL, err
+
+
 def test_config5_contexts_on_a_non_aliased_subset(cuda_device: torch.device) -> None:
     """Config 5's heavy-tailed contexts (logU[512, 32768]): its shortest, longest and quantile
     rows, each with its own blocks (no pool aliasing), against the fp32 oracle; automatic and

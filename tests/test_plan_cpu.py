@@ -187,6 +187,24 @@ def test_tc_split_fits_one_wave(rows) -> None:
     assert all(int(it[3]) % 8 == 0 for it in tcv)
 
 
+def test_decode_outliers_split_only_without_tensor_core_work() -> None:
+    """Decode rows beyond a wave stay whole, except that in a plan without tensor-core work the
+    rows longer than the pages per item-slot are split into pieces of about that size."""
+    rows = [(1, 100)] * 60 + [(1, 4000)] * 4
+    b = custom(rows, seed=4)
+    check_plan(b.chunks, b.num_tokens)
+    packed, info = plan_batch(b.chunks, b.num_tokens, 16, 148, 0)
+    _, dec, _, _, comb = decode_plan(packed, info)
+    assert info.pages_per_split < 512 and info.n_combine == 4
+    assert max(int(it[4] - it[3]) for it in dec) <= info.pages_per_split
+    assert all(int(it[4] - it[3]) == 7 for it in dec if int(it[0]) < 60)  # short rows whole
+    # The same rows beside a tensor-core chunk: nothing is split.
+    b2 = custom(rows + [(300, 0)], seed=4)
+    check_plan(b2.chunks, b2.num_tokens)
+    _, info2 = plan_batch(b2.chunks, b2.num_tokens, 16, 148, 0)
+    assert info2.n_combine == 0 and info2.n_decode_items == 64
+
+
 def test_empty_batch() -> None:
     packed, info = plan_batch([], 0)
     assert info.n_decode_items == info.n_tile_items == info.n_combine == 0
