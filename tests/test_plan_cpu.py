@@ -21,8 +21,8 @@ def decode_plan(packed: np.ndarray, info):
             recs(info.off_combine, info.n_combine))
 
 
-def check_plan(chunks: list[SeqChunk], num_tokens: int, split: int = 0) -> None:
-    packed, info = plan_batch(chunks, num_tokens, 16, 148, split)
+def check_plan(chunks: list[SeqChunk], num_tokens: int, split: int = 0, num_sms: int = 148) -> None:
+    packed, info = plan_batch(chunks, num_tokens, 16, num_sms, split)
     seqs, dec, til, tcv, comb = decode_plan(packed, info)
     assert info.num_seqs == len(chunks)
     flat_tables = packed[info.off_tables :]
@@ -203,6 +203,25 @@ def test_decode_outliers_split_only_without_tensor_core_work() -> None:
     check_plan(b2.chunks, b2.num_tokens)
     _, info2 = plan_batch(b2.chunks, b2.num_tokens, 16, 148, 0)
     assert info2.n_combine == 0 and info2.n_decode_items == 64
+
+
+@pytest.mark.parametrize("num_sms", [1, 7, 132, 148, 296])
+@pytest.mark.parametrize("seed", range(4))
+def test_plan_cover_for_other_sm_counts(num_sms: int, seed: int) -> None:
+    """The automatic splits (decode, tile, tensor-core, outlier rows) depend on the SM count; the
+    plan must stay a complete, disjoint cover for any of them, mixed batches and cascade groups
+    included."""
+    rng = np.random.default_rng(100 + seed)
+    rows = []
+    for _ in range(int(rng.integers(1, 60))):
+        kind = rng.integers(0, 5)
+        n = (1 if kind <= 1 else int(rng.integers(2, 9)) if kind == 2
+             else int(rng.integers(9, 65)) if kind == 3 else int(rng.integers(65, 700)))
+        rows.append((n, int(rng.integers(0, 6000))))
+    b = custom(rows, seed=seed)
+    check_plan(b.chunks, b.num_tokens, 0, num_sms)
+    c4 = config4(seed=seed, num_seqs=40)
+    check_plan(c4.chunks, c4.num_tokens, 0, num_sms)
 
 
 def test_empty_batch() -> None:
