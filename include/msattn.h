@@ -181,8 +181,9 @@ MS_API int ms_paged_attention(const void* q, int64_t q_row_stride, void* out, in
  *  - A plan needing more than MS_NOALLOC_SCRATCH_BYTES of partials
  *    (plan->workspace_bytes_per_kv_head * num_kv_heads) is rejected with MS_ERR_CAPACITY; plan
  *    with a larger pages_per_split or use ms_paged_attention.
- *  - The first call on a device looks up that device's address of the array (with that device
- *    current); make that first call before any stream capture.
+ *  - Every call looks up the current context's address of the array (with that device current),
+ *    so a context recreated after cudaDeviceReset gets the new address.  The first call in a
+ *    process may load the library's device code; make that first call before any stream capture.
  *  - All calls share the array: calls that overlap on the GPU race on it; calls ordered on one
  *    stream are safe.  No state carries over between calls. */
 #define MS_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)

@@ -62,7 +62,7 @@ class AttentionMetadata:
         need = int(self.info.workspace_bytes_per_kv_head) * num_kv_heads
         if need == 0:
             return None
-        key = (device.index if device.index is not None else torch.cuda.current_device(), num_kv_heads)
+        key = (str(device), num_kv_heads)  # a tensor's device always carries its index
         ws = self._workspace.get(key)
         if ws is None:
             ws = torch.empty(need, dtype=torch.uint8, device=device)
@@ -74,6 +74,8 @@ _SM_COUNT: dict[int, int] = {}
 
 
 def _num_sms(device: torch.device) -> int:
+    if device.type != "cuda":
+        raise RuntimeError("miniserve_b200 attention runs on CUDA only (no CPU fallback)")
     idx = device.index if device.index is not None else torch.cuda.current_device()
     if idx not in _SM_COUNT:
         _SM_COUNT[idx] = torch.cuda.get_device_properties(idx).multi_processor_count
@@ -179,16 +181,20 @@ def build_attention_metadata(
 ) -> AttentionMetadata:
     """Plan one step and upload it (one pinned H2D copy, no sync).  backends.py:80-98."""
     device = slot_mapping.device
-    if device.type != "cuda":
-        raise RuntimeError("miniserve_b200 attention runs on CUDA only (no CPU fallback)")
+    num_sms = _num_sms(device)  # raises for a non-CUDA device: there is no CPU path
     if block_size != BLOCK_SIZE:
         raise ValueError(f"block_size must be {BLOCK_SIZE}")
     num_tokens = int(slot_mapping.shape[0])
-    packed, info = plan_batch(chunks, num_tokens, block_size, _num_sms(device), pages_per_split)
-    host = torch.from_numpy(packed).pin_memory()
-    plan = host.to(device, non_blocking=True)
+    packed, info = plan_batch(chunks, num_tokens, block_size, num_sms, pages_per_split)
+    plan = _upload_plan(packed, device)
     slots = slot_mapping if slot_mapping.dtype == torch.int64 else slot_mapping.to(torch.int64)
     return AttentionMetadata(slots.contiguous(), plan, info, num_tokens)
+
+
+def _upload_plan(packed: np.ndarray, device: torch.device) -> Tensor:
+    """The step's one host-to-device copy: the packed plan, through pinned memory, non-blocking
+    (the reference's ``to_device``, utils.py:11-20)."""
+    return torch.from_numpy(packed).pin_memory().to(device, non_blocking=True)
 
 
 def _stream(device: torch.device) -> int:

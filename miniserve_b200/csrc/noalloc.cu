@@ -15,7 +15,6 @@
 // previous call's leftovers are never read.
 #include <cuda_runtime.h>
 
-#include <mutex>
 #include <string>
 
 #include "../../include/msattn.h"
@@ -29,37 +28,19 @@ namespace {
 // Split-KV partials: [part_rows][kv_heads][128] fp32 followed by [part_rows][kv_heads] fp32.
 static __device__ __align__(256) unsigned char g_noalloc_scratch[MS_NOALLOC_SCRATCH_BYTES];
 
-constexpr int kMaxDevices = 64;
-std::mutex g_mutex;
-void* g_scratch_addr[kMaxDevices] = {};
-
-// Device address of this device's copy of the array.  In host code the array's name only
-// stands for it; the real address comes from the runtime, once per device, with that device
-// current.
+// Device address of the current context's copy of the array.  In host code the array's name
+// only stands for it; the runtime gives the real address for the device that is current.  It is
+// looked up on every call (cheap once the module is loaded), so a context that was destroyed and
+// created again (cudaDeviceReset) never sees a stale address.
 int scratch_address(void** out) {
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) {
-    ms_host::set_error(std::string("ms_paged_attention_noalloc: cudaGetDevice: ") +
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+  if (e != cudaSuccess || p == nullptr) {
+    ms_host::set_error(std::string("ms_paged_attention_noalloc: cudaGetSymbolAddress: ") +
                        cudaGetErrorString(e));
     return MS_ERR_CUDA;
   }
-  if (dev < 0 || dev >= kMaxDevices) {
-    ms_host::set_error("ms_paged_attention_noalloc: device index out of range");
-    return MS_ERR_ARG;
-  }
-  std::lock_guard<std::mutex> lock(g_mutex);
-  if (g_scratch_addr[dev] == nullptr) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (e != cudaSuccess || p == nullptr) {
-      ms_host::set_error(std::string("ms_paged_attention_noalloc: cudaGetSymbolAddress: ") +
-                         cudaGetErrorString(e));
-      return MS_ERR_CUDA;
-    }
-    g_scratch_addr[dev] = p;
-  }
-  *out = g_scratch_addr[dev];
+  *out = p;
   return MS_OK;
 }
 

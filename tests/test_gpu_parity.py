@@ -17,8 +17,12 @@ import torch
 
 from golden.cases import CASES, D, EPS, H, KVH, THETA, random_inputs
 from golden_io import load_golden, make_inputs, run_oracle
-from miniserve_b200.workloads import Batch, config3, config4, custom
-from gpu_harness import bf16_ulp_diff, covered_rows, run_layer
+from gpu_harness import bf16_ulp_diff, covered_rows, run_layer, setup_pool
+from miniserve_b200 import _capi
+from miniserve_b200.attention import attend, build_attention_metadata, kv_scatter
+from miniserve_b200.kv_pool import allocate_kv_cache, layer_as_slots
+from miniserve_b200.qwen3_attention import qk_norm_rope_scatter
+from miniserve_b200.workloads import Batch, config2, config3, config4, custom
 from oracle import attention_oracle as orc
 
 pytestmark = pytest.mark.gpu
@@ -53,6 +57,12 @@ def test_kernel_a_matches_reference_bits(name: str, cuda_device: torch.device) -
         ulps = bf16_ulp_diff(got[key].cpu(), ref[key])
         assert int(ulps.max()) <= 1, key
         assert float((ulps > 0).float().mean()) <= 1e-3, key
+    # The whole pool against the reference's pool after its index_copy_ (backends.py:159-160):
+    # V everywhere and K in every slot this step does not write are bit-identical.
+    written = torch.zeros(ref["k_cache"].shape[0], dtype=torch.bool)
+    written[torch.from_numpy(inp.batch.slots)] = True
+    assert torch.equal(got["v_slots"].cpu(), ref["v_cache"])
+    assert torch.equal(got["k_slots"].cpu()[~written], ref["k_cache"][~written])
 
 
 @pytest.mark.parametrize("name", [c for c in CASES if c.endswith("bf16")])
@@ -231,3 +241,83 @@ def test_table_positions_mode_equals_gathered_rows(cuda_device: torch.device) ->
     rows = covered_rows(inp).to(cuda_device)
     assert torch.equal(a["q_rot"], b["q_rot"])
     assert torch.equal(a["out"][rows], b["out"][rows])
+
+
+@pytest.mark.parametrize("strided", [False, True], ids=["contiguous", "qkv_views"])
+@pytest.mark.parametrize("name", ["mixed_bf16", "prefix_verify_bf16", "groups_bf16", "prefill_bf16"])
+def test_kv_scatter_whole_pool_bit_exact(name: str, strided: bool,
+                                         cuda_device: torch.device) -> None:
+    """ms_kv_scatter (the reference's scatter, backends.py:159-160) against index_copy_ on the
+    reference-layout pool: every slot of the pool, written or not, is bit-identical.  With
+    ``strided`` the K/V rows are views into a fused [T, 4096] projection output, as the
+    reference's split (qwen3.py:94) hands them over."""
+    inp = make_inputs(name)
+    b = inp.batch
+    _pool, k_cache, v_cache = setup_pool(inp, cuda_device)
+    t = b.num_tokens
+    g = torch.Generator().manual_seed(99)
+    if strided:
+        qkv = torch.randn(t, (H + 2 * KVH) * D, generator=g).bfloat16()
+        k = qkv[:, H * D:(H + KVH) * D].view(t, KVH, D)
+        v = qkv[:, (H + KVH) * D:].view(t, KVH, D)
+        k_dev = qkv.to(cuda_device)[:, H * D:(H + KVH) * D].view(t, KVH, D)
+        v_dev = qkv.to(cuda_device)[:, (H + KVH) * D:].view(t, KVH, D)
+    else:
+        k = torch.randn(t, KVH, D, generator=g).bfloat16()
+        v = torch.randn(t, KVH, D, generator=g).bfloat16()
+        k_dev, v_dev = k.to(cuda_device), v.to(cuda_device)
+    slots = torch.from_numpy(b.slots)
+    kv_scatter(k_dev, v_dev, slots.to(cuda_device), k_cache, v_cache)
+    assert _capi.device_status(int(torch.cuda.current_stream(cuda_device).cuda_stream)) == 0
+    ref_k = inp.k_slots.clone()
+    ref_v = inp.v_slots.clone()
+    ref_k.index_copy_(0, slots, k.contiguous())
+    ref_v.index_copy_(0, slots, v.contiguous())
+    assert torch.equal(layer_as_slots(k_cache).cpu(), ref_k)
+    assert torch.equal(layer_as_slots(v_cache).cpu(), ref_v)
+
+
+@torch.no_grad()
+def test_config2_full_geometry_vs_fp32_oracle(cuda_device: torch.device) -> None:
+    """Config 2 exactly as bench.py times it (256 decode rows, contexts U[256, 4096], a pool of
+    1.1x the blocks needed with permuted tables, the automatic plan: one unsplit item per row)
+    for one layer: kernel A then kernels B/C, against the oracle's attention in fp32 over the same
+    bf16 queries and pool (run with PyTorch's plain fp32 math on the GPU; no TF32)."""
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+
+    dev = cuda_device
+    batch = config2(seed=1000)
+    nb, t = batch.num_blocks, batch.num_tokens
+    g = torch.Generator(device=dev).manual_seed(2)
+    pool, views = allocate_kv_cache(1, nb, KVH, dev, zero=False)
+    pool.normal_(generator=g)
+    k_cache, v_cache = views[0]
+    qkv = torch.randn(t, (H + 2 * KVH) * D, generator=g, device=dev).bfloat16()
+    qw = (1 + 0.1 * torch.randn(D, generator=g, device=dev)).bfloat16()
+    kw = (1 + 0.1 * torch.randn(D, generator=g, device=dev)).bfloat16()
+    cos_t, sin_t = orc.rope_tables(D, batch.max_position + 8, THETA)
+    positions = torch.from_numpy(batch.positions)
+    slots = torch.from_numpy(batch.slots).to(dev)
+    meta = build_attention_metadata(batch.chunks, slots, 16)
+    assert meta.info.n_decode_items == 256 and meta.info.n_combine == 0
+    assert meta.info.n_tc_items == 0 and meta.info.n_tile_items == 0
+    q = qk_norm_rope_scatter(qkv, qw, kw, EPS, cos_t[positions].to(dev), sin_t[positions].to(dev),
+                             slots, k_cache, v_cache, H)
+    out = attend(q, k_cache, v_cache, meta, D**-0.5)
+    assert _capi.device_status(int(torch.cuda.current_stream(dev).cuda_stream)) == 0
+
+    ks = layer_as_slots(k_cache).float()
+    vs = layer_as_slots(v_cache).float()
+    chunks = [orc.SeqChunk(c.flat_start, c.num_new, c.num_cached, list(c.block_table))
+              for c in batch.chunks]
+    ometa = orc.build_metadata(chunks, slots, 16)
+    allow = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        with sdpa_kernel(SDPBackend.MATH):
+            ref = orc.paged_attention(q.float(), ks[slots], vs[slots], ks, vs, ometa, D**-0.5)
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = allow
+    err = (out.float() - ref).abs().max().item()
+    print(f"config 2, {t} rows, {batch.kv_tokens_read()} context tokens: max-abs err {err:.3e}")
+    assert err <= ATOL, err

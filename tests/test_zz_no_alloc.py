@@ -6,8 +6,9 @@ cudaMalloc's implicit synchronisation).  Instead of a caller-provided workspace 
 split-KV partials in a fixed 16 MiB array built into the library.  These tests call it through
 the C ABI with ctypes and compare it with the regular entry point, ms_paged_attention, on a plan
 that splits almost every tile (so the scratch is really used), twice in a row (the second call
-runs over the first call's leftovers).  They also check that a plan too big for the array is
-refused before anything is launched.
+runs over the first call's leftovers).  Both run the same kernels on the same plan, so their rows
+must be bit-identical; the regular entry point is itself checked against the fp32 oracle.  They
+also check that a plan too big for the array is refused before anything is launched.
 
 This file is named so that pytest collects it last.
 """
@@ -24,6 +25,7 @@ from golden_io import make_inputs
 from gpu_harness import covered_rows, setup_pool
 from miniserve_b200 import _capi
 from miniserve_b200.attention import attend, build_attention_metadata, plan_batch
+from miniserve_b200.kv_pool import layer_as_slots
 from miniserve_b200.qwen3_attention import qk_norm_rope_scatter
 from miniserve_b200.workloads import custom
 from oracle import attention_oracle as orc
@@ -32,6 +34,18 @@ pytestmark = pytest.mark.gpu
 
 ATOL = 2e-2  # the attention tolerance used by the other parity tests
 SCRATCH_BYTES = 16 * 1024 * 1024
+
+
+def _fp32_oracle_out(inp, q: torch.Tensor, k_cache: torch.Tensor,
+                     v_cache: torch.Tensor) -> torch.Tensor:
+    """The oracle's attention in fp32 over the bf16 queries and pool the kernels read."""
+    ks = layer_as_slots(k_cache).float().cpu()
+    vs = layer_as_slots(v_cache).float().cpu()
+    slots = torch.from_numpy(inp.batch.slots)
+    chunks = [orc.SeqChunk(c.flat_start, c.num_new, c.num_cached, list(c.block_table))
+              for c in inp.batch.chunks]
+    meta = orc.build_metadata(chunks, slots, 16)
+    return orc.paged_attention(q.float().cpu(), ks[slots], vs[slots], ks, vs, meta, 128**-0.5)
 
 
 def _noalloc(q: torch.Tensor, out: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
@@ -64,14 +78,19 @@ def test_noalloc_matches_workspace_entry_point_twice(cuda_device: torch.device) 
 
     expected = attend(q, k_cache, v_cache, meta, scale)
     rows = covered_rows(inp).to(cuda_device)
+    # The regular entry point against the fp32 oracle on the same bf16 queries and pool, so the
+    # exact comparisons below compare with a checked result.
+    ref32 = _fp32_oracle_out(inp, q, k_cache, v_cache)
+    err32 = (expected[rows].float().cpu() - ref32[rows.cpu()]).abs().max().item()
+    assert err32 <= ATOL, err32
     for call in range(2):
         got = torch.full_like(q, float("nan"))
         rc = _noalloc(q, got, k_cache, v_cache, meta, scale)
         _capi.check(rc, "ms_paged_attention_noalloc")
         torch.cuda.synchronize(cuda_device)
         assert _capi.device_status(int(torch.cuda.current_stream(cuda_device).cuda_stream)) == 0
-        diff = (got[rows].float() - expected[rows].float()).abs().max().item()
-        assert diff <= ATOL, (call, diff)
+        # Same kernels on the same plan, only the scratch differs: bit-identical rows.
+        assert torch.equal(got[rows], expected[rows]), call
 
 
 def test_noalloc_rejects_plans_larger_than_its_scratch(cuda_device: torch.device) -> None:
