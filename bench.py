@@ -1,18 +1,22 @@
 """Benchmark of MiniServe's per-step paged-attention path on B200.
 
-Workload (config 2 of the path's benchmark set): one decode step of Qwen3-0.6B's attention path
-over all 28 layers for 256 sequences with context lengths U[256, 4096] (one new token each),
-16 query / 8 KV heads, head_dim 128, 16-token blocks, a KV pool of 1.1x the blocks needed per
-layer with randomly permuted block tables, N(0,1) bf16 values (synthetic; no model weights are
-involved on this path).  A "step" = for each of the 28 layers: kernel A (q/k RMSNorm + RoPE +
-K/V scatter) and kernels B/C (paged split-KV attention + combine).
+Headline workload (config 2 of the path's benchmark set): one decode step of Qwen3-0.6B's
+attention path over all 28 layers for 256 sequences per GPU with context lengths U[256, 4096]
+(one new token each), 16 query / 8 KV heads, head_dim 128, 16-token blocks, a KV pool of 1.1x
+the blocks needed per layer with randomly permuted block tables, N(0,1) bf16 values (synthetic;
+no model weights are involved on this path).  A "step" = for each of the 28 layers: kernel A
+(q/k RMSNorm + RoPE + K/V scatter) and the attention kernels (paged split-KV attention + combine).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-With N > 1 (launched by torchrun) every rank runs its own config-2 batch on its own GPU
-(sequences shard across GPUs with no data-path collective: weak scaling); the time is the max
-over ranks.  ``--impl reference`` times the reference algorithm (the CPU oracle restating
-MiniServe's torch code) on the host cores instead.
+With N > 1 (launched by torchrun) the global batch is N x 256 rows -- N copies of the single-GPU
+batch's context lengths -- sharded over the ranks by context tokens (greedy LPT), so every GPU
+streams the same bytes as at N = 1 (weak scaling) with no data-path collective; the time is the
+max over ranks.  The same line also reports, as extra keys, config 3 (mixed prefill, the
+tensor-core kernel), config 4 (shared prefix + speculative verify, the cascade path) and config 5
+(box scale: 8,192 rows sharded over the N GPUs, strong scaling), each with its own roofline.
+``--impl reference`` times the reference algorithm (the CPU oracle restating MiniServe's torch
+code) on the host cores on the same batch.
 
 Rank 0 prints one JSON line.
 """
@@ -38,7 +42,8 @@ sys.path.insert(0, str(ROOT))
 LAYERS = 28
 H, KVH, D = 16, 8, 128
 METRIC = "decode tok/s (paged-attn path, 28 layers, config 2)"
-PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+SEED = 1000  # every workload's batch geometry (config 5: its own seed 0)
 
 
 def parse() -> argparse.Namespace:
@@ -60,8 +65,10 @@ def parse() -> argparse.Namespace:
                    default="cfg2",
                    help="cfg2 is the headline; cfg1 (8 short decode rows), cfg3 (mixed prefill), "
                         "cfg4 (prefix + verify) and cfg5 (box scale: 8192 rows sharded over the "
-                        "ranks) are reported alongside; qkv times kernel E (qkv projection + "
-                        "norm/RoPE/scatter) beside cuBLAS + kernel A at --tokens tokens")
+                        "ranks) alone; qkv times kernel E (qkv projection + norm/RoPE/scatter) "
+                        "beside cuBLAS + kernel A at --tokens tokens")
+    p.add_argument("--no-extras", action="store_true",
+                   help="headline only: skip the config 3 / 4 / 5 keys")
     p.add_argument("--no-qkv-part", action="store_true",
                    help="skip timing kernel E (qkv projection + norm/RoPE/scatter) beside "
                         "cuBLAS + kernel A")
@@ -75,6 +82,13 @@ def peaks() -> tuple[dict, str]:
     if f.exists():
         return json.loads(f.read_text()), "measured"
     return PEAKS_FALLBACK, "fallback"
+
+
+def traffic_per_unit(key: str) -> dict | None:
+    f = ROOT / "profiles" / "traffic.json"
+    if not f.exists():
+        return None
+    return json.loads(f.read_text()).get(key)
 
 
 # ---------------------------------------------------------------------------------------------
@@ -100,6 +114,7 @@ class ClockSampler:
                 stdout=self.file, stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
+        time.sleep(0.3)
 
     def stop(self) -> dict:
         if self.proc is None:
@@ -132,12 +147,53 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------------------------------------
-# our implementation
+# workloads
 # ---------------------------------------------------------------------------------------------
 
 
+def make_batch(name: str, rank: int, world: int, seqs: int = 256, pool_gb: float = 150.0):
+    """This rank's batch of a workload.  Configs 1, 3 and 4 are single-GPU configurations: every
+    rank runs the same batch.  Config 2 shards N copies of the single-GPU batch, config 5 its
+    8,192 rows, by context tokens."""
+    from miniserve_b200.workloads import config1, config2, config3, config4, config5
+
+    if name == "cfg1":
+        return config1(seed=SEED)
+    if name == "cfg2":
+        return config2(seed=SEED, num_seqs=seqs, rank=rank, world=world)
+    if name == "cfg3":
+        return config3(seed=SEED)
+    if name == "cfg4":
+        return config4(seed=SEED)
+    return config5(rank, world, seed=0, pool_bytes=pool_gb * 1e9)
+
+
+def workload_label(name: str, world: int, seqs: int = 256, layers: int = LAYERS,
+                   pool_gb: float = 150.0) -> str:
+    return {
+        "cfg1": "config1: 8 decode seqs, ctx U[1,512], pool 1070 blocks",
+        "cfg2": (f"config2: {seqs} decode seqs/GPU (global batch {seqs * world}, LPT-sharded by "
+                 f"context tokens), ctx U[256,4096], 16q/8kv heads, d128, block 16, {layers} layers"),
+        "cfg3": "config3: 48 decode rows ctx U[128,2048] + 2 chunks x 1000 tokens over 512 cached",
+        "cfg4": ("config4: 512 rows sharing a 1024-token prefix (64 blocks), U[64,256] own tokens, "
+                 "5-token verify queries"),
+        "cfg5": (f"config5: 8192 decode seqs in total, ctx logU[512,32768], LPT-sharded by tokens "
+                 f"over {world} GPU(s), one {pool_gb:.0f} GB pool per GPU shared by the 28 layers"),
+    }[name]
+
+
+def headline_config(world: int, seqs: int, layers: int) -> dict:
+    """The `config` object of the headline line, identical in both arms."""
+    return {
+        "workload": workload_label("cfg2", world, seqs, layers),
+        "layers": layers,
+        "l2": "inputs larger than L2 (KV read per layer-step ~2.2 GB >> 126 MB)",
+        "parallelism": f"sequence-sharded x{world}, no data-path collective",
+    }
+
+
 def attention_bytes(batch) -> tuple[int, int, int]:
-    """Algorithmic bytes of one attention launch (kernels B+C), of one kernel-A launch, and the
+    """Algorithmic bytes of one attention launch (kernels B+C/D), of one kernel-A launch, and the
     attention FLOPs (causal pairs only).
 
     Attention bytes: every distinct physical KV block's K and V of each KV head once (bf16; a
@@ -154,6 +210,173 @@ def attention_bytes(batch) -> tuple[int, int, int]:
     kern_a = t * (H + 2 * KVH) * D * 2 + t * H * D * 2 + t * 2 * KVH * D * 2 + t * D * 4 * 2 + t * 8
     pairs = sum(c.num_new * c.num_cached + c.num_new * (c.num_new + 1) // 2 for c in batch.chunks)
     return attn, kern_a, 4 * D * H * pairs
+
+
+class DeviceStep:
+    """One workload's step on this GPU: ``layers`` x (kernel A, attention), every input resident
+    in HBM, the plan built and uploaded once (it is per step, shared by the layers)."""
+
+    def __init__(self, batch, layers: int, device: torch.device, pages_per_split: int = 0,
+                 seed: int = 1234) -> None:
+        from miniserve_b200.attention import build_attention_metadata
+        from miniserve_b200.kv_pool import allocate_kv_cache
+        from miniserve_b200.workloads import rope_tables
+
+        self.batch, self.layers, self.device = batch, layers, device
+        self.alias = bool(getattr(batch, "aliased", False)) or batch.name.startswith("cfg5")
+        t = batch.num_tokens
+        g = torch.Generator(device=device).manual_seed(seed)
+        self.pool, views = allocate_kv_cache(1 if self.alias else layers, batch.num_blocks, KVH,
+                                             device, zero=False)
+        for layer in range(self.pool.shape[0]):
+            self.pool[layer].normal_(generator=g)
+        # Config 5: one pool shared by all layers (it cannot hold 28 separate ones).
+        self.views = views * layers if self.alias else views
+        self.qkv_all = torch.randn(layers, t, (H + 2 * KVH) * D, generator=g, device=device,
+                                   dtype=torch.bfloat16)
+        self.qw = (1 + 0.1 * torch.randn(layers, D, generator=g, device=device)).bfloat16()
+        self.kw = (1 + 0.1 * torch.randn(layers, D, generator=g, device=device)).bfloat16()
+        self.cos_t, self.sin_t = rope_tables(D, batch.max_position + 8, 1e6, device)
+        positions = torch.from_numpy(batch.positions).to(device)
+        self.slot_mapping = torch.from_numpy(batch.slots).to(device)
+        self.cos, self.sin = self.cos_t[positions], self.sin_t[positions]
+        self.pages_per_split = pages_per_split
+        self.meta = build_attention_metadata(batch.chunks, self.slot_mapping, 16,
+                                             pages_per_split=pages_per_split)
+        self.q_buf = torch.empty(t, H, D, dtype=torch.bfloat16, device=device)
+        self.out_all = torch.empty(layers, t, H, D, dtype=torch.bfloat16, device=device)
+        self.stream = torch.cuda.current_stream(device)
+        info = self.meta.info
+        self.launches_per_layer = (1 + (info.n_decode_items > 0) + (info.n_tile_items > 0)
+                                   + (info.n_tc_items > 0) + (info.n_combine > 0))
+        self.ev_attn = [[torch.cuda.Event(enable_timing=True) for _ in range(2)]
+                        for _ in range(layers)]
+        self.graph: torch.cuda.CUDAGraph | None = None
+
+    def step(self, timed_kernels: bool = False) -> None:
+        from miniserve_b200.attention import attend
+        from miniserve_b200.qwen3_attention import qk_norm_rope_scatter
+
+        for layer in range(self.layers):
+            k_cache, v_cache = self.views[layer]
+            qk_norm_rope_scatter(self.qkv_all[layer], self.qw[layer], self.kw[layer], 1e-6,
+                                 self.cos, self.sin, self.slot_mapping, k_cache, v_cache, H,
+                                 q_out=self.q_buf)
+            if timed_kernels:
+                self.ev_attn[layer][0].record(self.stream)
+            attend(self.q_buf, k_cache, v_cache, self.meta, D**-0.5, out=self.out_all[layer])
+            if timed_kernels:
+                self.ev_attn[layer][1].record(self.stream)
+
+    def check_status(self, when: str) -> None:
+        from miniserve_b200 import _capi
+
+        status = _capi.device_status(int(self.stream.cuda_stream))
+        if status:
+            raise RuntimeError(f"device status {status:#x} {when}")
+
+    def capture(self) -> None:
+        """The whole step as one CUDA graph (the C-ABI calls neither allocate nor synchronise)."""
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.step()
+        for _ in range(2):
+            self.graph.replay()
+        torch.cuda.synchronize(self.device)
+
+    def timed(self, fn, steps: int, world: int) -> float:
+        """Milliseconds for ``steps`` calls of ``fn``: barrier + synchronize on both sides, CUDA
+        events on the launching stream."""
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize(self.device)
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(self.stream)
+        for _ in range(steps):
+            fn()
+        stop.record(self.stream)
+        torch.cuda.synchronize(self.device)
+        return start.elapsed_time(stop)
+
+    def attention_launch_ms(self, reps: int) -> float:
+        """Mean CUDA-event duration of the attention launches (events around each layer's
+        attention call, on the stream it launches on)."""
+        ms: list[float] = []
+        for _ in range(max(1, reps)):
+            self.step(timed_kernels=True)
+            torch.cuda.synchronize(self.device)
+            ms.extend(self.ev_attn[layer][0].elapsed_time(self.ev_attn[layer][1])
+                      for layer in range(self.layers))
+        return float(np.mean(ms))
+
+    def part_us(self, chunks, reps: int = 10) -> float:
+        """One attention call over a subset of the rows, alone: CUDA-graph replay of ``reps``
+        calls on layer 0's pool, microseconds per call."""
+        from miniserve_b200.attention import attend, build_attention_metadata
+
+        k_cache, v_cache = self.views[0]
+        sub_meta = build_attention_metadata(chunks, self.slot_mapping, 16,
+                                            pages_per_split=self.pages_per_split)
+        attend(self.q_buf, k_cache, v_cache, sub_meta, D**-0.5, out=self.out_all[0])
+        torch.cuda.synchronize(self.device)
+        g_sub = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_sub):
+            for _ in range(reps):
+                attend(self.q_buf, k_cache, v_cache, sub_meta, D**-0.5, out=self.out_all[0])
+        g_sub.replay()
+        torch.cuda.synchronize(self.device)
+        best = float("inf")
+        for _ in range(3):
+            p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            p0.record(self.stream)
+            g_sub.replay()
+            p1.record(self.stream)
+            torch.cuda.synchronize(self.device)
+            best = min(best, p0.elapsed_time(p1) * 1e3 / reps)
+        del g_sub
+        return best
+
+    def release(self) -> None:
+        self.graph = None
+        for name in ("pool", "views", "qkv_all", "out_all", "q_buf", "meta", "cos", "sin"):
+            setattr(self, name, None)
+        torch.cuda.synchronize(self.device)
+        torch.cuda.empty_cache()
+
+
+def roofline_hbm(kernel: str, nbytes: float, us: float, traffic: float | None) -> dict:
+    pk, src = peaks()
+    hbm = float(pk["hbm_gbs"])
+    achieved = nbytes / (us * 1e-6) / 1e9
+    return {"kernel": kernel, "bound": "hbm", "achieved": achieved, "peak": hbm,
+            "peak_source": f"{src} (hbm_gbs: copy bandwidth)", "unit": "GB/s",
+            "frac": achieved / hbm, "traffic": traffic, "algorithmic_bytes_per_launch": nbytes}
+
+
+def roofline_tensor(kernel: str, flops: float, us: float, traffic: float | None) -> dict:
+    pk, src = peaks()
+    burst = float(pk["bf16_tflops"])
+    sustained = float(pk.get("bf16_tflops_sustained", burst))
+    achieved = flops / (us * 1e-6) / 1e12
+    return {"kernel": kernel, "bound": "tensor", "achieved": achieved, "peak": burst,
+            "peak_source": f"{src} (bf16_tflops: cuBLAS GEMM burst; timed alone)",
+            "unit": "TFLOP/s", "frac": achieved / burst,
+            "frac_of_sustained": achieved / sustained, "peak_sustained": sustained,
+            "traffic": traffic, "algorithmic_flops_per_launch": flops}
+
+
+def scaled_traffic(key: str, units: float) -> float | None:
+    """ncu's DRAM bytes for a kernel, per unit of its work (from profiles/traffic.json), times
+    the units this launch processes."""
+    t = traffic_per_unit(key)
+    if not t:
+        return None
+    return float(t["bytes_per_unit"]) * units
+
+
+# ---------------------------------------------------------------------------------------------
+# our implementation: the headline
+# ---------------------------------------------------------------------------------------------
 
 
 def time_qkv_projection(t: int, views, qw, kw, cos, sin, slot_mapping, layers: int,
@@ -258,164 +481,19 @@ def run_qkv_only(args: argparse.Namespace, rank: int, device: torch.device) -> N
                       "qkv_projection": r}), flush=True)
 
 
-def run_ours(args: argparse.Namespace, rank: int, world: int, device: torch.device) -> dict:
-    from miniserve_b200 import _capi
-    from miniserve_b200.attention import attend, build_attention_metadata
-    from miniserve_b200.kv_pool import allocate_kv_cache
+def run_e2e(ws: DeviceStep, args: argparse.Namespace, world: int) -> tuple[float, int, int]:
+    """The same step through the public Python API with host buffers: each step prepares its
+    positions and slot mapping from the block tables (ms_prepare_step), plans (ms_plan_build)
+    and uploads the plan, copies every layer's qkv up from pinned host memory and every layer's
+    output back.  Returns (ms for args.steps steps, H2D bytes per step, D2H bytes per step)."""
+    from miniserve_b200.attention import attend, build_attention_metadata, prepare_arrays
     from miniserve_b200.qwen3_attention import qk_norm_rope_scatter
-    from miniserve_b200.workloads import (config1, config2, config3, config4, config5,
-                                          rope_tables)
 
-    alias_layers = False
-    if args.workload == "cfg1":
-        batch = config1(seed=1000 + rank)
-    elif args.workload == "cfg2":
-        batch = config2(seed=1000 + rank, num_seqs=args.seqs)
-    elif args.workload == "cfg3":
-        batch = config3(seed=1000 + rank)
-    elif args.workload == "cfg4":
-        batch = config4(seed=1000 + rank)
-    else:
-        batch = config5(rank, world, seed=0, pool_bytes=args.pool_gb * 1e9)
-        alias_layers = True  # one pool shared by all layers (it cannot hold 28 separate ones)
-    LAYERS = args.layers
-    t = batch.num_tokens
-    g = torch.Generator(device=device).manual_seed(1234 + rank)
-    pool, views = allocate_kv_cache(1 if alias_layers else LAYERS, batch.num_blocks, KVH, device,
-                                    zero=False)
-    for layer in range(pool.shape[0]):
-        pool[layer].normal_(generator=g)
-    if alias_layers:
-        views = views * LAYERS
-    qkv_all = torch.randn(LAYERS, t, (H + 2 * KVH) * D, generator=g, device=device,
-                          dtype=torch.bfloat16)
-    qw = (1 + 0.1 * torch.randn(LAYERS, D, generator=g, device=device)).bfloat16()
-    kw = (1 + 0.1 * torch.randn(LAYERS, D, generator=g, device=device)).bfloat16()
-    cos_t, sin_t = rope_tables(D, batch.max_position + 8, 1e6, device)
-    positions = torch.from_numpy(batch.positions).to(device)
-    slot_mapping = torch.from_numpy(batch.slots).to(device)
-    cos, sin = cos_t[positions], sin_t[positions]
-    meta = build_attention_metadata(batch.chunks, slot_mapping, 16,
-                                    pages_per_split=args.pages_per_split)
-    q_buf = torch.empty(t, H, D, dtype=torch.bfloat16, device=device)
-    out_all = torch.empty(LAYERS, t, H, D, dtype=torch.bfloat16, device=device)
-    stream = torch.cuda.current_stream(device)
-    scale = D**-0.5
-    info = meta.info
-    launches_per_layer = (1 + (info.n_decode_items > 0) + (info.n_tile_items > 0)
-                          + (info.n_tc_items > 0) + (info.n_combine > 0))
-
-    ev_attn = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(LAYERS)]
-
-    def step(timed_kernels: bool = False) -> None:
-        for layer in range(LAYERS):
-            k_cache, v_cache = views[layer]
-            qk_norm_rope_scatter(qkv_all[layer], qw[layer], kw[layer], 1e-6, cos, sin,
-                                 slot_mapping, k_cache, v_cache, H, q_out=q_buf)
-            if timed_kernels:
-                ev_attn[layer][0].record(stream)
-            attend(q_buf, k_cache, v_cache, meta, scale, out=out_all[layer])
-            if timed_kernels:
-                ev_attn[layer][1].record(stream)
-
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize(device)
-    status = _capi.device_status(int(stream.cuda_stream))
-    if status:
-        raise RuntimeError(f"device status {status:#x} after warm-up")
-
-    # The whole 28-layer step is captured once as a CUDA graph (the C-ABI calls neither allocate
-    # nor synchronise) and replayed; the eager time is reported beside it.
-    graph = None
-    if not args.no_graph:
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            step()
-        for _ in range(2):
-            graph.replay()
-        torch.cuda.synchronize(device)
-
-    def timed(fn) -> float:
-        if world > 1:
-            torch.distributed.barrier()
-        torch.cuda.synchronize(device)
-        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        start.record(stream)
-        for _ in range(args.steps):
-            fn()
-        stop.record(stream)
-        torch.cuda.synchronize(device)
-        return start.elapsed_time(stop)
-
-    # ---- timed region: device-resident inputs ----
-    sampler = ClockSampler(device.index if device.index is not None else 0) if rank == 0 else None
-    if sampler:
-        sampler.start()
-        time.sleep(0.3)
-    attn_ms: list[float] = []
-    eager_ms = timed(step)
-    total_ms = timed(graph.replay) if graph is not None else eager_ms
-    # per-kernel durations (same work, events around each attention launch)
-    for _ in range(max(1, min(args.steps, 5))):
-        step(timed_kernels=True)
-        torch.cuda.synchronize(device)
-        attn_ms.extend(ev_attn[layer][0].elapsed_time(ev_attn[layer][1]) for layer in range(LAYERS))
-    clocks = sampler.stop() if sampler else None
-    if world > 1:
-        torch.distributed.barrier()
-    status = _capi.device_status(int(stream.cuda_stream))
-    if status:
-        raise RuntimeError(f"device status {status:#x} after timing")
-
-    # ---- config 3's two parts, timed apart (decode rows; prefill chunks) ----
-    parts = None
-    dec_chunks = [c for c in batch.chunks if c.num_new <= 64]
-    pre_chunks = [c for c in batch.chunks if c.num_new > 64]
-    if dec_chunks and pre_chunks:
-        parts = {}
-        k_cache, v_cache = views[0]
-        for name, sub in (("decode_rows", dec_chunks), ("prefill_chunks", pre_chunks)):
-            sub_meta = build_attention_metadata(sub, slot_mapping, 16,
-                                                pages_per_split=args.pages_per_split)
-            attend(q_buf, k_cache, v_cache, sub_meta, scale, out=out_all[0])
-            torch.cuda.synchronize(device)
-            g_sub = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g_sub):
-                for _ in range(10):
-                    attend(q_buf, k_cache, v_cache, sub_meta, scale, out=out_all[0])
-            g_sub.replay()
-            torch.cuda.synchronize(device)
-            p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            p0.record(stream)
-            g_sub.replay()
-            p1.record(stream)
-            torch.cuda.synchronize(device)
-            us = p0.elapsed_time(p1) * 1e3 / 10
-            del g_sub
-            sub_batch = type(batch)(batch.name, sub, batch.num_blocks)
-            sub_bytes, _, sub_flops = attention_bytes(sub_batch)
-            parts[name] = {"us_per_layer": us, "GB/s": sub_bytes / (us * 1e-6) / 1e9,
-                           "TFLOPS_causal": sub_flops / (us * 1e-6) / 1e12,
-                           "timing": "CUDA-graph replay of 10 calls, this part alone"}
-
-    qkv_part = None
-    if not args.no_qkv_part and rank == 0:
-        qkv_part = time_qkv_projection(t, views, qw, kw, cos, sin, slot_mapping, LAYERS, device,
-                                       stream)
-        status = _capi.device_status(int(stream.cuda_stream))
-        if status:
-            raise RuntimeError(f"device status {status:#x} after the qkv projection timing")
-
-    # ---- e2e: through the public API with host buffers ----
-    qkv_host = qkv_all.cpu().pin_memory()
-    out_host = torch.empty(LAYERS, t, H, D, dtype=torch.bfloat16).pin_memory()
-    qkv_dev = torch.empty_like(qkv_all)
-
-    # Host preparation each step, as an engine runs it: positions and slot mappings from the
-    # block tables (ms_prepare_step, into alternating pinned buffers), then the plan.
-    from miniserve_b200.attention import prepare_arrays
-
+    device, stream, batch = ws.device, ws.stream, ws.batch
+    layers, t = ws.layers, batch.num_tokens
+    qkv_host = ws.qkv_all.cpu().pin_memory()
+    out_host = torch.empty(layers, t, H, D, dtype=torch.bfloat16).pin_memory()
+    qkv_dev = torch.empty_like(ws.qkv_all)
     n_seq = len(batch.chunks)
     new_np = np.fromiter((c.num_new for c in batch.chunks), dtype=np.int32, count=n_seq)
     cached_np = np.fromiter((c.num_cached for c in batch.chunks), dtype=np.int32, count=n_seq)
@@ -427,9 +505,9 @@ def run_ours(args: argparse.Namespace, rank: int, world: int, device: torch.devi
     copies_done: list = [None, None]
     step_no = [0]
     copy_stream = torch.cuda.Stream(device)
-    qkv_arrived = [torch.cuda.Event() for _ in range(LAYERS)]
-    qkv_consumed = [torch.cuda.Event() for _ in range(LAYERS)]
-    out_written = [torch.cuda.Event() for _ in range(LAYERS)]
+    qkv_arrived = [torch.cuda.Event() for _ in range(layers)]
+    qkv_consumed = [torch.cuda.Event() for _ in range(layers)]
+    out_written = [torch.cuda.Event() for _ in range(layers)]
     first_step = [True]
     step_started = torch.cuda.Event()
     overlap_copies = qkv_host[0].numel() * 2 >= (1 << 20)  # per-layer copies of >= 1 MiB
@@ -446,17 +524,17 @@ def run_ours(args: argparse.Namespace, rank: int, world: int, device: torch.devi
         done = torch.cuda.Event()
         done.record(stream)
         copies_done[k] = done
-        m = build_attention_metadata(batch.chunks, slots_d, 16, pages_per_split=args.pages_per_split)
-        c, s = cos_t[pos_d], sin_t[pos_d]
+        m = build_attention_metadata(batch.chunks, slots_d, 16, pages_per_split=ws.pages_per_split)
+        c, s = ws.cos_t[pos_d], ws.sin_t[pos_d]
         if not overlap_copies:
             # Small steps: two bulk copies cost less host time than per-layer stream choreography.
             qkv_dev.copy_(qkv_host, non_blocking=True)
-            for layer in range(LAYERS):
-                k_cache, v_cache = views[layer]
-                q = qk_norm_rope_scatter(qkv_dev[layer], qw[layer], kw[layer], 1e-6, c, s, slots_d,
-                                         k_cache, v_cache, H, q_out=q_buf)
-                attend(q, k_cache, v_cache, m, scale, out=out_all[layer])
-            out_host.copy_(out_all, non_blocking=True)
+            for layer in range(layers):
+                k_cache, v_cache = ws.views[layer]
+                q = qk_norm_rope_scatter(qkv_dev[layer], ws.qw[layer], ws.kw[layer], 1e-6, c, s,
+                                         slots_d, k_cache, v_cache, H, q_out=ws.q_buf)
+                attend(q, k_cache, v_cache, m, D**-0.5, out=ws.out_all[layer])
+            out_host.copy_(ws.out_all, non_blocking=True)
             return
         # Each layer's qkv goes up, and its output comes back, on a copy stream, overlapped with
         # the other layers' kernels (as a serving engine pipelines them); the step ends when the
@@ -464,65 +542,218 @@ def run_ours(args: argparse.Namespace, rank: int, world: int, device: torch.devi
         step_started.record(stream)  # no copy of this step may run before the step begins
         with torch.cuda.stream(copy_stream):
             copy_stream.wait_event(step_started)
-            for layer in range(LAYERS):
+            for layer in range(layers):
                 if not first_step[0]:
                     copy_stream.wait_event(qkv_consumed[layer])
                 qkv_dev[layer].copy_(qkv_host[layer], non_blocking=True)
                 qkv_arrived[layer].record(copy_stream)
-        for layer in range(LAYERS):
-            k_cache, v_cache = views[layer]
+        for layer in range(layers):
+            k_cache, v_cache = ws.views[layer]
             stream.wait_event(qkv_arrived[layer])
-            q = qk_norm_rope_scatter(qkv_dev[layer], qw[layer], kw[layer], 1e-6, c, s, slots_d,
-                                     k_cache, v_cache, H, q_out=q_buf)
+            q = qk_norm_rope_scatter(qkv_dev[layer], ws.qw[layer], ws.kw[layer], 1e-6, c, s,
+                                     slots_d, k_cache, v_cache, H, q_out=ws.q_buf)
             qkv_consumed[layer].record(stream)
-            attend(q, k_cache, v_cache, m, scale, out=out_all[layer])
+            attend(q, k_cache, v_cache, m, D**-0.5, out=ws.out_all[layer])
             out_written[layer].record(stream)
             with torch.cuda.stream(copy_stream):
                 copy_stream.wait_event(out_written[layer])
-                out_host[layer].copy_(out_all[layer], non_blocking=True)
+                out_host[layer].copy_(ws.out_all[layer], non_blocking=True)
         stream.wait_stream(copy_stream)
         first_step[0] = False
 
     for _ in range(max(1, args.warmup)):
         e2e_step()
     torch.cuda.synchronize(device)
+    e2e_ms = ws.timed(e2e_step, args.steps, world)
+    h2d = qkv_host.numel() * 2 + pos_bufs[0].numel() * 8 + slot_bufs[0].numel() * 8 \
+        + int(ws.meta.info.total_ints) * 4
+    d2h = out_host.numel() * 2
+    return e2e_ms, h2d, d2h
+
+
+def run_headline(args: argparse.Namespace, rank: int, world: int, device: torch.device) -> dict:
+    batch = make_batch(args.workload, rank, world, args.seqs, args.pool_gb)
+    ws = DeviceStep(batch, args.layers, device, args.pages_per_split, seed=1234 + rank)
+    for _ in range(args.warmup):
+        ws.step()
+    torch.cuda.synchronize(device)
+    ws.check_status("after warm-up")
+    if not args.no_graph:
+        ws.capture()
+
+    # ---- timed region: device-resident inputs ----
+    sampler = ClockSampler(device.index if device.index is not None else 0) if rank == 0 else None
+    if sampler:
+        sampler.start()
+    eager_ms = ws.timed(ws.step, args.steps, world)
+    total_ms = ws.timed(ws.graph.replay, args.steps, world) if ws.graph is not None else eager_ms
+    attn_ms = ws.attention_launch_ms(min(args.steps, 5))
+    clocks = sampler.stop() if sampler else None
     if world > 1:
         torch.distributed.barrier()
-    e_start, e_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e_start.record(stream)
-    for _ in range(args.steps):
-        e2e_step()
-    e_stop.record(stream)
-    torch.cuda.synchronize(device)
-    e2e_ms = e_start.elapsed_time(e_stop)
-    h2d = qkv_host.numel() * 2 + pos_bufs[0].numel() * 8 + slot_bufs[0].numel() * 8 + int(info.total_ints) * 4
-    d2h = out_host.numel() * 2
+    ws.check_status("after timing")
 
+    # ---- a mixed batch's two parts, timed apart (decode rows; prefill chunks) ----
+    parts = None
+    dec_chunks = [c for c in batch.chunks if c.num_new <= 64]
+    pre_chunks = [c for c in batch.chunks if c.num_new > 64]
+    if dec_chunks and pre_chunks:
+        parts = {}
+        for name, sub in (("decode_rows", dec_chunks), ("prefill_chunks", pre_chunks)):
+            us = ws.part_us(sub)
+            sub_bytes, _, sub_flops = attention_bytes(type(batch)(batch.name, sub, batch.num_blocks))
+            parts[name] = {"us_per_layer": us, "GB/s": sub_bytes / (us * 1e-6) / 1e9,
+                           "TFLOPS_causal": sub_flops / (us * 1e-6) / 1e12,
+                           "timing": "CUDA-graph replay of 10 calls, this part alone"}
+
+    qkv_part = None
+    if not args.no_qkv_part and rank == 0:
+        qkv_part = time_qkv_projection(batch.num_tokens, ws.views, ws.qw, ws.kw, ws.cos, ws.sin,
+                                       ws.slot_mapping, ws.layers, device, ws.stream)
+        ws.check_status("after the qkv projection timing")
+
+    e2e_ms, h2d, d2h = run_e2e(ws, args, world)
     attn_bytes, a_bytes, attn_flops = attention_bytes(batch)
-    return {
-        "total_ms": total_ms,
-        "eager_ms": eager_ms,
-        "graph": graph is not None,
-        "e2e_ms": e2e_ms,
-        "attn_ms": float(np.mean(attn_ms)),
-        "attn_bytes": attn_bytes,
-        "attn_flops": attn_flops,
-        "logical_kv_tokens": batch.kv_tokens_read(),
-        "kernel_a_bytes": a_bytes,
-        "tokens": t,
-        "kv_tokens": (batch.kv_tokens_read() if getattr(batch, "aliased", False)
-                      else batch.unique_kv_tokens()),
-        "pool_shared_by_layers": alias_layers,
-        "num_blocks": batch.num_blocks,
-        "clocks": clocks,
-        "launches_per_step": LAYERS * launches_per_layer,
-        "h2d": h2d,
-        "d2h": d2h,
-        "parts": parts,
-        "qkv_projection": qkv_part,
+    info = ws.meta.info
+    res = {
+        "total_ms": total_ms, "eager_ms": eager_ms, "graph": ws.graph is not None,
+        "e2e_ms": e2e_ms, "attn_ms": attn_ms, "attn_bytes": attn_bytes,
+        "attn_flops": attn_flops, "logical_kv_tokens": batch.kv_tokens_read(),
+        "kernel_a_bytes": a_bytes, "tokens": batch.num_tokens,
+        "kv_tokens": (batch.kv_tokens_read() if ws.alias else batch.unique_kv_tokens()),
+        "pool_shared_by_layers": ws.alias, "num_blocks": batch.num_blocks, "clocks": clocks,
+        "launches_per_step": ws.layers * ws.launches_per_layer, "h2d": h2d, "d2h": d2h,
+        "parts": parts, "qkv_projection": qkv_part,
         "plan": {"decode_items": info.n_decode_items, "tile_items": info.n_tile_items,
                  "tc_items": info.n_tc_items, "combine": info.n_combine,
-                 "pages_per_split": info.pages_per_split},
+                 "cascade_groups": info.n_cascade, "pages_per_split": info.pages_per_split},
+    }
+    ws.release()
+    return res
+
+
+# ---------------------------------------------------------------------------------------------
+# our implementation: the other configurations, reported beside the headline
+# ---------------------------------------------------------------------------------------------
+
+
+def run_single_gpu_config(name: str, args: argparse.Namespace, device: torch.device) -> dict:
+    """Config 3 or 4 on this GPU: the 28-layer step (CUDA-graph replay) and its attention
+    launches, each with the roofline of the kernel that dominates it."""
+    steps, warmup = max(3, min(args.steps, 20)), max(3, args.warmup)
+    batch = make_batch(name, 0, 1)
+    ws = DeviceStep(batch, LAYERS, device, 0, seed=77)
+    for _ in range(warmup):
+        ws.step()
+    torch.cuda.synchronize(device)
+    ws.check_status(f"after the {name} warm-up")
+    ws.capture()
+    total_ms = ws.timed(ws.graph.replay, steps, 1)
+    attn_ms = ws.attention_launch_ms(3)
+    ws.check_status(f"after the {name} timing")
+    attn_bytes, _, attn_flops = attention_bytes(batch)
+    info = ws.meta.info
+    out = {
+        "workload": workload_label(name, 1),
+        "us_per_layer_step": total_ms * 1e3 / (steps * LAYERS),
+        "tokens_per_s": batch.num_tokens * steps / (total_ms * 1e-3),
+        "attn_us_per_layer": attn_ms * 1e3,
+        "timing": f"CUDA-graph replay of the 28-layer step x {steps} after {warmup} warm-up steps; "
+                  "attention launches timed with CUDA events around each layer's call",
+        "plan": {"decode_items": info.n_decode_items, "tile_items": info.n_tile_items,
+                 "tc_items": info.n_tc_items, "combine": info.n_combine,
+                 "cascade_groups": info.n_cascade},
+    }
+    if name == "cfg3":
+        dec = [c for c in batch.chunks if c.num_new <= 64]
+        pre = [c for c in batch.chunks if c.num_new > 64]
+        pre_us, dec_us = ws.part_us(pre), ws.part_us(dec)
+        pre_batch = type(batch)(batch.name, pre, batch.num_blocks)
+        dec_batch = type(batch)(batch.name, dec, batch.num_blocks)
+        _, _, pre_flops = attention_bytes(pre_batch)
+        dec_bytes, _, _ = attention_bytes(dec_batch)
+        pre_q = sum(c.num_new for c in pre)
+        out["prefill_part"] = {
+            "us_per_layer": pre_us,
+            "roofline": roofline_tensor("prefill_tc_kernel (kernel D, tcgen05/TMEM): the two "
+                                        "1000-token chunks", pre_flops, pre_us,
+                                        scaled_traffic("prefill_tc_cfg3", pre_q)),
+            "timing": "CUDA-graph replay of 10 attention calls over the prefill chunks alone",
+        }
+        out["decode_part"] = {
+            "us_per_layer": dec_us,
+            "roofline": roofline_hbm("paged_attn_kernel decode mode: the 48 decode rows",
+                                     dec_bytes, dec_us, None),
+            "timing": "CUDA-graph replay of 10 attention calls over the decode rows alone",
+        }
+        out["roofline"] = out["prefill_part"]["roofline"]
+    else:
+        # Cascade: the shared prefix once on the tensor-core kernel, every row's own pages on the
+        # persistent decode kernel; bytes count each physical block once (logical bytes beside).
+        logical = (batch.kv_tokens_read() * KVH * D * 2 * 2 + batch.num_tokens * H * D * 2 * 2)
+        out["roofline"] = roofline_hbm(
+            "cascade attention: prefill_tc_kernel (shared prefix once) + "
+            "paged_decode_units_kernel (own pages, merged)", attn_bytes, attn_ms * 1e3,
+            scaled_traffic("cascade_cfg4", batch.num_tokens))
+        out["roofline"]["logical_bytes_per_launch"] = logical
+        out["roofline"]["logical_GBps"] = logical / (attn_ms * 1e-3) / 1e9
+    ws.release()
+    return out
+
+
+def run_config5(args: argparse.Namespace, rank: int, world: int, device: torch.device) -> dict:
+    """Config 5 (box scale) at this N: the 8,192 rows sharded over the ranks by context tokens
+    (strong scaling), a pool of about 150 GB per GPU shared by the 28 layers.  Time = max over
+    ranks of the 28-layer step; per-rank roofline from each rank's own bytes and time."""
+    steps, warmup = max(3, min(args.steps, 5)), 3
+    batch = make_batch("cfg5", rank, world, pool_gb=args.pool_gb)
+    ws = DeviceStep(batch, LAYERS, device, 0, seed=55 + rank)
+    for _ in range(warmup):
+        ws.step()
+    torch.cuda.synchronize(device)
+    ws.check_status("after the config-5 warm-up")
+    ws.capture()
+    sampler = ClockSampler(device.index if device.index is not None else 0) if rank == 0 else None
+    if sampler:
+        sampler.start()
+    total_ms = ws.timed(ws.graph.replay, steps, world)
+    clocks = sampler.stop() if sampler else None
+    attn_ms = ws.attention_launch_ms(1)
+    ws.check_status("after the config-5 timing")
+    attn_bytes, _, _ = attention_bytes(batch)
+    mine = torch.tensor([total_ms / steps, attn_ms, attn_bytes / (attn_ms * 1e-3) / 1e9,
+                         batch.num_tokens, batch.kv_tokens_read()], dtype=torch.float64,
+                        device=device)
+    every = [torch.zeros_like(mine) for _ in range(world)]
+    if world > 1:
+        torch.distributed.all_gather(every, mine)
+    else:
+        every = [mine]
+    rows = [x.cpu().tolist() for x in every]
+    ws.release()
+    step_ms = max(r[0] for r in rows)
+    hbm = float(peaks()[0]["hbm_gbs"])
+    per_rank = [{"rank": i, "ms_per_step": r[0], "attn_us_per_layer": r[1] * 1e3,
+                 "achieved_GBps": r[2], "frac": r[2] / hbm, "rows": int(r[3]),
+                 "kv_tokens_per_layer": int(r[4])} for i, r in enumerate(rows)]
+    slowest = min(per_rank, key=lambda r: r["achieved_GBps"])
+    return {
+        "workload": workload_label("cfg5", world, pool_gb=args.pool_gb),
+        "scaling": "strong",
+        "value": 8192 / (step_ms * 1e-3),
+        "unit": "tok/s",
+        "ms_per_step": step_ms,
+        "us_per_layer_step": step_ms * 1e3 / LAYERS,
+        "timing": f"CUDA-graph replay of the 28-layer step x {steps} after {warmup} warm-up "
+                  "steps; max over ranks",
+        "roofline": {**roofline_hbm("paged_attn_kernel decode mode + combine (each rank's "
+                                    "share; logical bytes, the shared pool is >> L2)",
+                                    slowest["achieved_GBps"] * 1.0, 1e6, None),
+                     "achieved": slowest["achieved_GBps"], "frac": slowest["frac"],
+                     "algorithmic_bytes_per_launch": None,
+                     "note": "slowest rank's attention launches: its bytes / its CUDA-event time"},
+        "per_rank": per_rank,
+        "clocks": clocks,
     }
 
 
@@ -531,19 +762,15 @@ def run_ours(args: argparse.Namespace, rank: int, world: int, device: torch.devi
 # ---------------------------------------------------------------------------------------------
 
 
-def cpu_reference_layer_setup(num_seqs: int, seed: int = 0):
-    """One layer of config 2 in the reference's own layout and dtype, on the host."""
-    from miniserve_b200.workloads import config2
+def cpu_reference_layer_setup(batch, seed: int = 0):
+    """One layer of a batch in the reference's own layout and dtype, on the host: the same
+    geometry, pool size and block tables as the GPU arm."""
     from oracle import attention_oracle as orc
 
-    batch = config2(seed=seed, num_seqs=num_seqs)
-    # Compact pool: only the blocks the batch uses, renumbered densely (same geometry).
-    used = sorted({b for c in batch.chunks for b in c.block_table})
-    remap = {b: i for i, b in enumerate(used)}
-    chunks = [orc.SeqChunk(c.flat_start, c.num_new, c.num_cached, [remap[b] for b in c.block_table])
+    chunks = [orc.SeqChunk(c.flat_start, c.num_new, c.num_cached, list(c.block_table))
               for c in batch.chunks]
     g = torch.Generator().manual_seed(seed)
-    nslots = len(used) * 16
+    nslots = batch.num_blocks * 16
     t = batch.num_tokens
     k_cache = torch.randn(nslots, KVH, D, generator=g).bfloat16()
     v_cache = torch.randn(nslots, KVH, D, generator=g).bfloat16()
@@ -551,9 +778,8 @@ def cpu_reference_layer_setup(num_seqs: int, seed: int = 0):
     qw = (1 + 0.1 * torch.randn(D, generator=g)).bfloat16()
     kw = (1 + 0.1 * torch.randn(D, generator=g)).bfloat16()
     cos, sin = orc.rope_tables(D, batch.max_position + 8, 1e6)
-    slots = torch.tensor([s for c in chunks for s in orc.slots_for(c, 16)], dtype=torch.long)
-    positions = torch.tensor([p for c in chunks for p in range(c.num_cached, c.context_len)],
-                             dtype=torch.long)
+    slots = torch.from_numpy(batch.slots)
+    positions = torch.from_numpy(batch.positions)
 
     def layer() -> None:
         meta = orc.build_metadata(chunks, slots, 16)
@@ -562,23 +788,25 @@ def cpu_reference_layer_setup(num_seqs: int, seed: int = 0):
     return layer, t
 
 
-def run_cpu_layers(num_seqs: int, warmup: int, iters: int | None, budget_s: float | None):
+def run_cpu_layers(batch, warmup: int, iters: int) -> tuple[float, int, int, int]:
+    """Median seconds of one layer of the reference's CPU path (all host threads), after
+    ``warmup`` untimed runs; the same policy serves the reference arm and the cpu_baseline."""
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    layer, t = cpu_reference_layer_setup(num_seqs)
+    layer, t = cpu_reference_layer_setup(batch)
     for _ in range(warmup):
         layer()
     times = []
-    t_end = time.perf_counter() + (budget_s or 0)
-    while True:
+    for _ in range(iters):
         t0 = time.perf_counter()
         layer()
         times.append(time.perf_counter() - t0)
-        if iters is not None and len(times) >= iters:
-            break
-        if budget_s is not None and time.perf_counter() >= t_end:
-            break
-    return float(np.mean(times)), t, threads, len(times)
+    return float(statistics.median(times)), t, threads, len(times)
+
+
+CPU_SAMPLE = ("each sample = 1 of the 28 layers of this rank-0 batch (norm + RoPE + scatter + "
+              "metadata + gathered SDPA, the oracle restating MiniServe's torch path) on the "
+              "host CPU; median of the samples; tok/s = tokens / (28 x median)")
 
 
 # ---------------------------------------------------------------------------------------------
@@ -593,7 +821,8 @@ def main() -> None:
     if args.impl == "reference":
         if rank != 0:
             return
-        t_layer, t, threads, n = run_cpu_layers(args.seqs, args.warmup, args.steps, None)
+        batch = make_batch("cfg2", 0, max(world, args.gpus), args.seqs)
+        t_layer, t, threads, n = run_cpu_layers(batch, max(3, args.warmup), args.steps)
         value = t / (LAYERS * t_layer)
         line = {
             "impl": "reference",
@@ -602,19 +831,19 @@ def main() -> None:
             "unit": "tok/s",
             "n_gpus": args.gpus,
             "steps": args.steps,
-            "warmup": args.warmup,
-            "ms_per_step": t_layer * LAYERS * 1e3,
+            "warmup": max(3, args.warmup),
+            "ms_per_step": t_layer * 1e3,
+            "step": "one bounded sample: 1 of the 28 layers of the batch",
+            "ms_per_layer": t_layer * 1e3,
+            "ms_per_28_layers_extrapolated": t_layer * LAYERS * 1e3,
             "higher_is_better": True,
-            "scaling": "strong" if args.workload == "cfg5" else "weak",
+            "scaling": "weak",
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic",
-            "config": {"workload": f"config2: {args.seqs} decode seqs, ctx U[256,4096], 28 layers",
-                       "parallelism": "host cores"},
+            "config": headline_config(max(world, args.gpus), args.seqs, LAYERS),
             "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port",
-                             "sample": "each step = 1 of 28 layers of the full batch, on the "
-                                       "host CPU, time x28 (oracle restating MiniServe's torch "
-                                       "path)"},
+                             "sample": CPU_SAMPLE + f"; {n} samples"},
             "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0},
         }
@@ -644,37 +873,56 @@ def main() -> None:
             torch.distributed.destroy_process_group()
         return
 
-    r = run_ours(args, rank, world, device)
+    r = run_headline(args, rank, world, device)
+    hbm = float(peaks()[0]["hbm_gbs"])
+    my_achieved = r["attn_bytes"] / (r["attn_ms"] * 1e-3) / 1e9
     ms = torch.tensor([r["total_ms"], r["e2e_ms"], r["attn_ms"], r["eager_ms"]],
                       dtype=torch.float64, device=device)
     toks = torch.tensor([r["tokens"]], dtype=torch.float64, device=device)
+    mine = torch.tensor([my_achieved, r["attn_ms"], r["attn_bytes"]], dtype=torch.float64,
+                        device=device)
+    every = [torch.zeros_like(mine) for _ in range(world)]
     if world > 1:
         torch.distributed.all_reduce(ms, op=torch.distributed.ReduceOp.MAX)
         torch.distributed.all_reduce(toks, op=torch.distributed.ReduceOp.SUM)
-    total_ms, e2e_ms, attn_ms, eager_ms = (float(x) for x in ms.cpu())
+        torch.distributed.all_gather(every, mine)
+    else:
+        every = [mine]
+    per_rank = [x.cpu().tolist() for x in every]
+    total_ms, e2e_ms, attn_ms_max, eager_ms = (float(x) for x in ms.cpu())
     ms_per_step = total_ms / args.steps
     e2e_per_step = e2e_ms / args.steps
     tokens_all = int(toks.item())
 
+    headline = args.workload == "cfg2" and args.layers == LAYERS
+    extras: dict = {}
+    if headline and not args.no_extras:
+        # Configs 3 and 4 are single-GPU configurations: rank 0 runs them while the others wait.
+        if rank == 0:
+            extras["config3"] = run_single_gpu_config("cfg3", args, device)
+            extras["config4"] = run_single_gpu_config("cfg4", args, device)
+        if world > 1:
+            torch.distributed.barrier()
+        extras["config5"] = run_config5(args, rank, world, device)
+
     cpu = None
-    if (rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload == "cfg2"
-            and args.layers == LAYERS):
-        t_layer, t, threads, n = run_cpu_layers(args.seqs, 1, None, 12.0)
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and headline:
+        batch0 = make_batch("cfg2", 0, 1, args.seqs)
+        t_layer, t, threads, n = run_cpu_layers(batch0, 3, 20)
         cpu = {"value": t / (LAYERS * t_layer), "unit": "tok/s", "cores": threads, "kind": "port",
-               "sample": f"1 of 28 layers of the full config-2 batch, {n} timed runs on the host "
-                         "CPU (oracle restating MiniServe's torch path), time x28"}
+               "sample": CPU_SAMPLE + f"; {n} samples after 3 warm-up runs"}
 
     if rank == 0:
-        pk, src = peaks()
-        hbm = float(pk["hbm_gbs"])
-        achieved = r["attn_bytes"] / (attn_ms * 1e-3) / 1e9
-        traffic_file = ROOT / "profiles" / "traffic.json"
-        traffic = None
-        if traffic_file.exists():
-            traffic = json.loads(traffic_file.read_text()).get("paged_attn_decode_cfg2")
-        metric = METRIC if args.workload == "cfg2" else METRIC.replace("config 2", args.workload)
+        slowest = min(range(world), key=lambda i: per_rank[i][0])
+        achieved = per_rank[slowest][0]
+        if args.workload == "cfg2":
+            kernel = "paged_attn_kernel decode mode (kernel B; + combine C when a plan splits)"
+            units = r["kv_tokens"]
+            traffic = scaled_traffic("paged_attn_decode_cfg2", units)
+        else:
+            kernel, traffic = f"attention launches of {args.workload}", None
         line = {
-            "metric": metric,
+            "metric": METRIC if args.workload == "cfg2" else METRIC.replace("config 2", args.workload),
             "value": tokens_all / (ms_per_step * 1e-3),
             "unit": "tok/s",
             "n_gpus": world,
@@ -682,39 +930,31 @@ def main() -> None:
             "warmup": args.warmup,
             "ms_per_step": ms_per_step,
             "higher_is_better": True,
-            "scaling": "weak",
+            "scaling": "strong" if args.workload == "cfg5" else "weak",
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic",
-            "config": {
-                "workload": (f"config2: {args.seqs} decode seqs/GPU, ctx U[256,4096], 16q/8kv "
-                             f"heads, d128, block 16, {args.layers} layers"
-                             if args.workload == "cfg2" else
-                             "config5: 8192 decode seqs in total, ctx logU[512,32768], sharded by "
-                             f"tokens over {world} GPU(s), one {args.pool_gb:.0f} GB pool per GPU "
-                             "shared by the 28 layers" if args.workload == "cfg5" else args.workload),
-                "layers": args.layers,
-                "kv_tokens_per_layer": r["kv_tokens"],
-                "logical_kv_tokens_per_layer": r["logical_kv_tokens"],
-                "pool_blocks_per_layer": r["num_blocks"],
-                "l2": "inputs larger than L2 (KV read per layer-step >> 126 MB)",
-                "parallelism": f"sequence-sharded x{world}, no data-path collective",
-            },
+            "config": (headline_config(world, args.seqs, args.layers) if args.workload == "cfg2"
+                       else {"workload": workload_label(args.workload, world, args.seqs,
+                                                        args.layers, args.pool_gb),
+                             "layers": args.layers,
+                             "parallelism": f"sequence-sharded x{world}"}),
+            "workload_stats": {"kv_tokens_per_layer": r["kv_tokens"],
+                               "logical_kv_tokens_per_layer": r["logical_kv_tokens"],
+                               "pool_blocks_per_layer": r["num_blocks"],
+                               "tokens_per_rank": r["tokens"]},
             "us_per_layer_step": ms_per_step * 1e3 / args.layers,
             "step_timing": "CUDA-graph replay of the captured step" if r["graph"] else "eager",
             "eager_ms_per_step": eager_ms / args.steps,
-            "attn_us_per_layer": attn_ms * 1e3,
+            "attn_us_per_layer": attn_ms_max * 1e3,
             "roofline": {
-                "kernel": "paged attention decode (kernel B + combine C)",
-                "bound": "hbm",
+                **roofline_hbm(kernel, per_rank[slowest][2], per_rank[slowest][1] * 1e3, traffic),
                 "achieved": achieved,
-                "peak": hbm,
-                "peak_source": src,
-                "unit": "GB/s",
                 "frac": achieved / hbm,
-                "traffic": traffic,
-                "algorithmic_bytes_per_launch": r["attn_bytes"],
-                "attn_tflops": r["attn_flops"] / (attn_ms * 1e-3) / 1e12,
+                "per_rank_achieved": [x[0] for x in per_rank],
+                "note": "achieved = the slowest rank's algorithmic bytes / its mean attention "
+                        "launch time (CUDA events)",
+                "attn_tflops": r["attn_flops"] / (r["attn_ms"] * 1e-3) / 1e12,
             },
             "cpu_baseline": cpu,
             "e2e": {"value": tokens_all / (e2e_per_step * 1e-3), "unit": "tok/s",
@@ -732,6 +972,7 @@ def main() -> None:
             line["parts"] = r["parts"]
         if r["qkv_projection"] is not None:
             line["qkv_projection"] = r["qkv_projection"]
+        line.update(extras)
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.barrier()

@@ -103,10 +103,23 @@ def config1(seed: int = 0) -> Batch:
     return _assemble("cfg1", [(1, int(L) - 1) for L in ctx], rng, pool_blocks=1070)
 
 
-def config2(seed: int = 0, num_seqs: int = 256) -> Batch:
+def config2(seed: int = 0, num_seqs: int = 256, rank: int = 0, world: int = 1) -> Batch:
+    """256 decode rows, contexts U[256, 4096].  With ``world`` > 1 (weak scaling, fixed work per
+    GPU): one global batch of ``num_seqs * world`` rows whose contexts are ``world`` copies of the
+    single-GPU batch's, split over the ranks by context tokens (greedy LPT,
+    ``sharding.shard_by_tokens``), so every rank streams the single-GPU batch's KV bytes; each
+    rank's share gets its own pool and permuted tables.  With one rank it is the single-GPU batch
+    itself."""
+    from .sharding import shard_by_tokens
+
     rng = np.random.default_rng(seed)
     ctx = rng.integers(256, 4097, size=num_seqs)
-    return _assemble("cfg2", [(1, int(L) - 1) for L in ctx], rng)
+    if world == 1:
+        return _assemble("cfg2", [(1, int(L) - 1) for L in ctx], rng)
+    everyone = np.tile(ctx, world)
+    mine = shard_by_tokens(everyone.tolist(), world)[rank]
+    return _assemble(f"cfg2[{rank}/{world}]", [(1, int(everyone[i]) - 1) for i in mine],
+                     np.random.default_rng([seed, rank]))
 
 
 def config3(seed: int = 0) -> Batch:

@@ -321,3 +321,40 @@ def test_config2_full_geometry_vs_fp32_oracle(cuda_device: torch.device) -> None
     err = (out.float() - ref).abs().max().item()
     print(f"config 2, {t} rows, {batch.kv_tokens_read()} context tokens: max-abs err {err:.3e}")
     assert err <= ATOL, err
+
+
+def test_tensor_core_items_with_empty_tile_b_repeat_identically(cuda_device: torch.device) -> None:
+    """Items whose tile B is empty (n_b = 0) run on the tensor-core kernel in every plan with an
+    odd number of 64-token groups (the middle item of the zig-zag pairing) and for split-chunk
+    tails.  Twenty chunks of 129-192 tokens (three groups each) plus decode rows, automatic and
+    forced splits: 30 back-to-back calls give bit-identical outputs and a clean status, and the
+    result matches the fp32 oracle."""
+    from miniserve_b200.attention import plan_batch
+
+    rows = [(129 + 3 * i, 40 * i) for i in range(20)] + [(1, 500), (5, 90)]
+    batch = custom(rows, seed=71)
+    inp = random_inputs(batch, 71)
+    for split in (0, 8):
+        _, info = plan_batch(batch.chunks, batch.num_tokens, 16, 148, split)
+        assert info.n_tc_items > 0
+        got = run_layer(inp, cuda_device, pages_per_split=split)
+        assert int(got["status"]) == 0
+        rows_ = covered_rows(inp)
+        ref32 = _fp32_reference_out(inp, got["q_rot"], got["k_slots"], got["v_slots"])[rows_]
+        err = (got["out"].cpu()[rows_].float() - ref32).abs().max().item()
+        assert err <= ATOL, (split, err)
+        # Repeat the attention alone on the same pool and queries.
+        _pool, k_cache, v_cache = setup_pool(inp, cuda_device)
+        from miniserve_b200.kv_pool import slots_into_layer
+
+        slots_into_layer(k_cache, got["k_slots"])
+        slots_into_layer(v_cache, got["v_slots"])
+        slots = torch.from_numpy(batch.slots).to(cuda_device)
+        meta = build_attention_metadata(batch.chunks, slots, 16, pages_per_split=split)
+        first = attend(got["q_rot"], k_cache, v_cache, meta, D**-0.5)
+        dev_rows = rows_.to(cuda_device)
+        for _ in range(30):
+            again = attend(got["q_rot"], k_cache, v_cache, meta, D**-0.5)
+            assert torch.equal(again[dev_rows], first[dev_rows])
+        assert _capi.device_status(int(torch.cuda.current_stream(cuda_device).cuda_stream)) == 0
+        assert torch.equal(first[dev_rows], got["out"][dev_rows])
