@@ -198,6 +198,20 @@ static int ensure_smem_attrs() {
   e = cudaFuncSetAttribute(ms::prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            ms::TcCfg::kSmemBytes);
   if (e != cudaSuccess) return cuda_fail("cudaFuncSetAttribute(tc)", e);
+  {
+    // The tensor-core kernel moves registers between its warpgroups (setmaxnreg); the increase
+    // can only be met out of what the launch allocated, so a build that gave the kernel fewer
+    // registers per thread than the split assumes must never be launched.
+    cudaFuncAttributes fa{};
+    e = cudaFuncGetAttributes(&fa, ms::prefill_tc_kernel);
+    if (e != cudaSuccess) return cuda_fail("cudaFuncGetAttributes(tc)", e);
+    if (fa.numRegs < ms::TcCfg::kLaunchRegs) {
+      ms_host::set_error("prefill_tc_kernel was compiled with " + std::to_string(fa.numRegs) +
+                         " registers per thread; its register split needs " +
+                         std::to_string(ms::TcCfg::kLaunchRegs));
+      return MS_ERR_CUDA;
+    }
+  }
   e = cudaFuncSetAttribute(ms::qkv_proj_norm_rope_kernel<1>,
                            cudaFuncAttributeMaxDynamicSharedMemorySize, ms::QkvCfg<1>::kSmemBytes);
   if (e != cudaSuccess) return cuda_fail("cudaFuncSetAttribute(qkv 1)", e);

@@ -6,21 +6,22 @@
 // (tile A = tokens 0..63 of the item, tile B = tokens 64..127; row = token * 2 + head), and a
 // range of the sequence's KV pages, walked in blocks of 128 keys.
 //
-//   warps 0-3   softmax for tile A, warps 4-7 softmax for tile B: one thread per row (TMEM lane).
-//               Per block: read the row's 128 scores from TMEM, causal / range mask (cached length
-//               as offset), row max, p = 2^(s*scale*log2e - m) (2 of 8 pairs on the FMA pipe) for
-//               the first 64, a second read of the last 64 (registers do not hold 128 scores and 64
-//               packed P words at once), release of the S columns (the next S can start), the
-//               rest of p, row sum, and P packed to bf16 in registers; then, once this tile's
-//               previous P*V has finished with its P buffer in shared memory, P is stored there.
-//               The running max only moves (and O in TMEM is rescaled) when it grows by more
-//               than 2^8.
+//   warps 0-3   softmax for tile A, warps 4-7 softmax for tile B: one thread per row (TMEM lane),
+//               224 registers each (the producer / MMA warpgroup gives its registers up).
+//               Per block: read the row's 128 scores from TMEM and release the S columns at once
+//               (the next S then runs on the tensor core during this block's softmax), causal /
+//               range mask (cached length as offset), row max, p = 2^(s*scale*log2e - m) (2 of 8
+//               pairs on the FMA pipe), row sum, and P packed to bf16 in registers; then, once
+//               this tile's previous P*V has finished with its P buffer in shared memory, P is
+//               stored there.  The running max only moves (and O in TMEM is rescaled) when it
+//               grows by more than 2^8.
 //   warp 8      TMA producer: K and V blocks in consumption order K_0, K_1, V_0, K_2, V_1, ... into
 //               a 3-slot ring of 32 KiB.  K: 16 boxes of 2 KiB (8 pages x two 64-dim halves), laid
 //               out as [half][128 keys][64] for the K-major operand; V: 8 boxes of 4 KiB (one page
 //               each), read as an MN-major operand one page per 16-key step.  One box per lane;
 //               pages past the item's range are read from an out-of-range block id, which the TMA
 //               unit fills with zeros.
+//   warp 11     no role (completes the third warpgroup for the register reconfiguration).
 //   warps 9, 10 MMA issuers (warp 9 also allocates the 512 TMEM columns); every MMA takes both
 //               operands from shared memory, P included:
 //                 warp 9:  S_t(j) = Q_t K_j^T  (M=128, N=128, K=128) once tile t holds S_t(j-1)
@@ -44,7 +45,17 @@
 namespace ms {
 
 struct TcCfg {
-  static constexpr int kThreads = 352;
+  // 12 warps = 3 warpgroups: softmax tile A, softmax tile B, and producer / MMA issuers (warps
+  // 8-10; warp 11 only completes the warpgroup, which register reconfiguration works on).
+  static constexpr int kThreads = 384;
+  // Registers per thread: 168 at launch (65,536 / 384, rounded down to a multiple of 8); then
+  // the softmax warpgroups take 224 and the producer / MMA warpgroup keeps 56:
+  // 2 x 128 x 224 + 128 x 56 = 64,512 = 384 x 168, exactly the launch's allocation.
+  static constexpr int kLaunchRegs = 168;
+  static constexpr int kSoftmaxRegs = 224;
+  static constexpr int kOtherRegs = 56;
+  static_assert(2 * 128 * kSoftmaxRegs + 128 * kOtherRegs <= kThreads * kLaunchRegs,
+                "register split exceeds the launch allocation");
   static constexpr int kSlots = 3;          // K/V ring slots (one 128-key K or V block each)
   static constexpr int kTileTokens = 64;    // query tokens per 128-row tile
   static constexpr int kBlockKeys = 128;
@@ -114,14 +125,6 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c),
                "r"(d)
                : "memory");
-}
-
-// Forces the 16 words to be computed before any later volatile asm (such as a TMEM load), so
-// the compiler cannot keep their inputs alive across it.
-__device__ __forceinline__ void pin16(const uint32_t (&v)[16]) {
-  asm volatile("" ::"r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]),
-               "r"(v[7]), "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]),
-               "r"(v[14]), "r"(v[15]));
 }
 
 __device__ __forceinline__ float max128(const float (&s0)[32], const float (&s1)[32],
@@ -233,371 +236,357 @@ __global__ void __launch_bounds__(TcCfg::kThreads, 1)
   // Start-up overlaps: once the barriers exist the producer streams K and V at once, while the
   // softmax warps load Q and warp 9 allocates TMEM; only the first S waits for Q.
   __syncthreads();
-  if (warp == 9) {
-    tmem_alloc(tmem_holder, TcCfg::kTmemCols);
-    tmem_relinquish();
-    tc_fence_before();
-    if (lane == 0) mbar_arrive(tmem_ready);
-  }
-  if (warp < 8) {
-    // Q tiles into the swizzled K-major layout: 256 rows (2 tiles x 64 tokens x 2 heads) of 16
-    // chunks of 16 bytes; each load instruction of a warp covers two whole rows (512 contiguous
-    // bytes: one token's two heads), so the loads coalesce.  All 16 loads are issued before any
-    // store (a shared store between them would make each load wait for the previous one).
-    uint4 v[16];
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const int f = i * 256 + threadIdx.x;
-      const int t = f >> 11, r = (f >> 4) & 127, u = f & 15;
-      const bool valid = (r >> 1) < (t == 0 ? n_a : n_b);
-      const int tok = (t == 0 ? tok_a : tok_b) + (r >> 1);
-      const __nv_bfloat16* src = a.q + static_cast<long long>(flat_start + tok) * a.q_row_stride +
-                                 (kvh * kGroup + (r & 1)) * kHeadDim + u * 8;
-      v[i] = valid ? __ldg(reinterpret_cast<const uint4*>(src)) : make_uint4(0u, 0u, 0u, 0u);
-    }
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const int f = i * 256 + threadIdx.x;
-      const int t = f >> 11, r = (f >> 4) & 127, u = f & 15;
-      st_shared_v4(smem_u32(smem + TcCfg::kQOff + t * TcCfg::kQBytes) + tile128_off(r, u), v[i].x,
-                   v[i].y, v[i].z, v[i].w);
-    }
-    fence_proxy_async_smem();
-    mbar_arrive(q_ready);
-  }
   uint32_t tmem = 0;
-  bool tmem_ok = true;
-  if (warp != 8) {
-    tmem_ok = mbar_wait_fast(tmem_ready, 0, abort_flag);
+  // Waits until warp 9 has published the TMEM allocation; on a timeout records it and stops.
+  auto wait_tmem = [&]() -> bool {
+    const bool ok = mbar_wait_fast(tmem_ready, 0, abort_flag);
     tc_fence_after();
-    if (tmem_ok) {
+    if (ok) {
       tmem = *tmem_holder;
     } else if (lane == 0) {
       atomicOr(&g_status_word, kErrTimeout);
       *abort_flag = 1;
     }
-  }
-
-  if (warp == 8) {
-    // ---------------- TMA producer ----------------
-    // Position p goes to slot p % NS once every MMA that read position p - NS has finished.
-    // K: lanes 0..15 issue one 2 KiB box each (page lane / 2, 64-dim half lane % 2) into
-    // [half][128 keys][64]; V: lanes 0..7 issue one 4 KiB box each (page lane) into [page][half]
-    // [16 keys][64].
-    const int* table = a.tables + table_off + page_begin;
-    int ids_j = (lane < 8 && lane < npages) ? table[lane] : -1;           // block j's pages
-    int ids_j1 = (lane < 8 && 8 + lane < npages) ? table[8 + lane] : -1;  // block j + 1's
-    int issued = 0;
-    auto load = [&](int p, bool is_v, int ids, int j) -> bool {
-      const int s = p % NS;
-      int ok = 1;
-      if (!is_v && lane < 8 && j * 8 + lane < npages &&
-          static_cast<unsigned>(ids) >= static_cast<unsigned>(a.num_blocks))
-        atomicOr(&g_status_word, kErrBlock);
-      if (lane == 0) {
-        if (*abort_flag) ok = 0;
-        if (ok && p >= NS && !mbar_wait(&slot_empty[s], ((p / NS) - 1) & 1)) {
-          atomicOr(&g_status_word, kErrTimeout);
-          *abort_flag = 1;
-          ok = 0;
+    return ok;
+  };
+  // One branch per warpgroup role, each starting with its register budget (the compiler gives a
+  // branch the registers of the setmaxnreg that begins it).  The softmax warpgroups hold a whole
+  // 128-score block and its 64 packed P words at once; the producer and the MMA issuers need
+  // few registers.
+  if (warp >= 8) {
+    setmaxnreg_dec<TcCfg::kOtherRegs>();
+    if (warp == 8) {
+      // ---------------- TMA producer ----------------
+      // Position p goes to slot p % NS once every MMA that read position p - NS has finished.
+      // K: lanes 0..15 issue one 2 KiB box each (page lane / 2, 64-dim half lane % 2) into
+      // [half][128 keys][64]; V: lanes 0..7 issue one 4 KiB box each (page lane) into [page][half]
+      // [16 keys][64].
+      const int* table = a.tables + table_off + page_begin;
+      int ids_j = (lane < 8 && lane < npages) ? table[lane] : -1;           // block j's pages
+      int ids_j1 = (lane < 8 && 8 + lane < npages) ? table[8 + lane] : -1;  // block j + 1's
+      int issued = 0;
+      auto load = [&](int p, bool is_v, int ids, int j) -> bool {
+        const int s = p % NS;
+        int ok = 1;
+        if (!is_v && lane < 8 && j * 8 + lane < npages &&
+            static_cast<unsigned>(ids) >= static_cast<unsigned>(a.num_blocks))
+          atomicOr(&g_status_word, kErrBlock);
+        if (lane == 0) {
+          if (*abort_flag) ok = 0;
+          if (ok && p >= NS && !mbar_wait(&slot_empty[s], ((p / NS) - 1) & 1)) {
+            atomicOr(&g_status_word, kErrTimeout);
+            *abort_flag = 1;
+            ok = 0;
+          }
+          if (ok) mbar_arrive_expect_tx(&slot_full[s], TcCfg::kSlotBytes);
         }
-        if (ok) mbar_arrive_expect_tx(&slot_full[s], TcCfg::kSlotBytes);
-      }
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (!ok) return false;
-      uint8_t* slot = smem + TcCfg::kRingOff + s * TcCfg::kSlotBytes;
-      if (is_v) {
-        const int b = __shfl_sync(0xffffffffu, ids, lane & 7);
-        if (lane < 8) tma_load_5d_plain(slot + lane * kPageBytes, &v_map, &slot_full[s], 0, 0, 2, kvh, b);
-      } else {
-        const int b = __shfl_sync(0xffffffffu, ids, (lane & 15) >> 1);
-        if (lane < 16) {
-          const int pg = lane >> 1, half = lane & 1;
-          tma_load_5d_plain(slot + half * 16384 + pg * (kPageBytes / 2), &k_map, &slot_full[s], 0,
-                            0, half, kvh, b);
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) return false;
+        uint8_t* slot = smem + TcCfg::kRingOff + s * TcCfg::kSlotBytes;
+        if (is_v) {
+          const int b = __shfl_sync(0xffffffffu, ids, lane & 7);
+          if (lane < 8) tma_load_5d_plain(slot + lane * kPageBytes, &v_map, &slot_full[s], 0, 0, 2, kvh, b);
+        } else {
+          const int b = __shfl_sync(0xffffffffu, ids, (lane & 15) >> 1);
+          if (lane < 16) {
+            const int pg = lane >> 1, half = lane & 1;
+            tma_load_5d_plain(slot + half * 16384 + pg * (kPageBytes / 2), &k_map, &slot_full[s], 0,
+                              0, half, kvh, b);
+          }
         }
-      }
-      __syncwarp();
-      ++issued;
-      return true;
-    };
-    if (nblk > 0 && load(pos_k(0), false, ids_j, 0)) {
-      for (int j = 0; j < nblk; ++j) {
-        if (j + 1 < nblk && !load(pos_k(j + 1), false, ids_j1, j + 1)) break;
-        if (!load(pos_v(j), true, ids_j, j)) break;
-        ids_j = ids_j1;
-        ids_j1 = (lane < 8 && (j + 2) * 8 + lane < npages) ? table[(j + 2) * 8 + lane] : -1;
-      }
-    }
-    // No copy may still be landing when the CTA exits: wait for the last use of each slot.
-    if (lane == 0) {
-      for (int p = issued > NS ? issued - NS : 0; p < issued; ++p) {
-        if (!mbar_wait(&slot_full[p % NS], (p / NS) & 1)) {
-          atomicOr(&g_status_word, kErrTimeout);
-          break;
-        }
-      }
-    }
-  } else if (!tmem_ok) {
-    // The TMEM address never became visible (the status word says why): no MMA or softmax work.
-  } else if (warp == 9 || warp == 10) {
-    // ---------------- MMA issuers: warp 9 issues every S = Q K^T, warp 10 every O += P V ------
-    // Two issuing threads, two independent MMA streams (different TMEM columns and operands): the
-    // issue queue of one thread is shallow, so any wait in a single issuer would leave the tensor
-    // core idle; with two, one stream keeps it busy while the other waits.  tcgen05.commit tracks
-    // the MMAs of the committing thread only, so each stream signals its own barriers.
-    if (lane == 0) {
-      const bool is_pv = warp == 10;
-      constexpr uint32_t kIdescS = umma_idesc_bf16(128, 128, false);
-      constexpr uint32_t kIdescPV = umma_idesc_bf16(128, 128, true);
-      const uint32_t ring = smem_u32(smem + TcCfg::kRingOff);
-      bool ok = true;
-      auto wait_slot = [&](int p) -> bool {
-        return mbar_wait_mma(&slot_full[p % NS], (p / NS) & 1, abort_flag);
+        __syncwarp();
+        ++issued;
+        return true;
       };
-      // Descriptors are built once; operand offsets are added to their start-address field
-      // (shared-memory addresses >> 4 fit its 14 bits with room to spare).
-      const uint64_t dq = umma_smem_desc_sw128(smem_u32(smem + TcCfg::kQOff), 16, 1024);
-      const uint64_t dp = umma_smem_desc_sw128(smem_u32(smem + TcCfg::kPOff), 16, 1024);
-      const uint64_t dk = umma_smem_desc_sw128(ring, 16, 1024);
-      const uint64_t dv = umma_smem_desc_sw128(ring, 2048, 1024);  // [page][half][16 keys][64]
-      constexpr uint32_t kSlot16 = TcCfg::kSlotBytes >> 4;
-      if (!is_pv) {
-        // S_t(j) = Q_t K_j^T into tile t's S columns, as soon as tile t holds S_t(j-1) in
-        // registers and K_j has landed (and, for S(0), Q is stored).  The tiles are not coupled:
-        // each goes as soon as its own softmax has released its S columns.
-        ok = nblk == 0 || mbar_wait_mma(q_ready, 0, abort_flag);
-        for (int j = 0; ok && j < nblk; ++j) {
-          if (!(ok = wait_slot(pos_k(j)))) break;
-          const uint64_t kd = dk + (pos_k(j) % NS) * kSlot16;
-          for (int t = 0; ok && t < 2; ++t) {
-            if (j < nblk_t[t]) {
-              if (j > 0 && !(ok = mbar_wait_mma(&s_free[t], (j - 1) & 1, abort_flag))) break;
-              tc_fence_after();
-              const uint64_t qd = dq + t * (TcCfg::kQBytes >> 4);
-#pragma unroll
-              for (int kk = 0; kk < 8; ++kk) {
-                const uint32_t off = ((kk >> 2) * 16384 + (kk & 3) * 32) >> 4;
-                umma_bf16_ss(tmem + t * 128, qd + off, kd + off, kIdescS, kk > 0 ? 1u : 0u);
-              }
-              umma_commit(&s_full[t]);
-            }
-          }
-          if (!ok) break;
-          umma_commit(&slot_empty[pos_k(j) % NS]);
-        }
-      } else {
-        // O_t += P_t(j) V_j once tile t's P(j) is stored and V_j has landed.
-        for (int j = 0; ok && j < nblk; ++j) {
-          if (!(ok = wait_slot(pos_v(j)))) break;
-          const uint64_t vd = dv + (pos_v(j) % NS) * kSlot16;
-          for (int t = 0; ok && t < 2; ++t) {
-            if (j < nblk_t[t]) {
-              if (!(ok = mbar_wait_mma(&p_full[t], j & 1, abort_flag))) break;
-              tc_fence_after();
-#pragma unroll
-              for (int kk = 0; kk < 8; ++kk)
-                umma_bf16_ss(tmem + TcCfg::kOCol + t * 128,
-                             dp + t * (TcCfg::kQBytes >> 4) +
-                                 (((kk >> 2) * 16384 + (kk & 3) * 32) >> 4),
-                             vd + kk * (kPageBytes >> 4), kIdescPV, (j > 0 || kk > 0) ? 1u : 0u);
-              umma_commit(&pv_done[t]);
-            }
-          }
-          if (!ok) break;
-          umma_commit(&slot_empty[pos_v(j) % NS]);
+      if (nblk > 0 && load(pos_k(0), false, ids_j, 0)) {
+        for (int j = 0; j < nblk; ++j) {
+          if (j + 1 < nblk && !load(pos_k(j + 1), false, ids_j1, j + 1)) break;
+          if (!load(pos_v(j), true, ids_j, j)) break;
+          ids_j = ids_j1;
+          ids_j1 = (lane < 8 && (j + 2) * 8 + lane < npages) ? table[(j + 2) * 8 + lane] : -1;
         }
       }
-      if (!ok) {
-        atomicOr(&g_status_word, kErrTimeout);
-        *abort_flag = 1;
-      }
-      // Every MMA issued so far (by both issuers) must finish before TMEM is freed or the CTA
-      // exits: each issuer commits once to mma_drain (two arrivals complete it).
-      umma_commit(mma_drain);
-      if (!mbar_wait(mma_drain, 0)) atomicOr(&g_status_word, kErrTimeout);
-    }
-    __syncwarp();
-  } else {
-    // ---------------- softmax warpgroups: thread = row of tile t ----------------
-    const int t = warp >> 2;
-    const int r = threadIdx.x & 127;
-    const bool valid = (r >> 1) < (t == 0 ? n_a : n_b);
-    const int tok = (t == 0 ? tok_a : tok_b) + (r >> 1);
-    const int qpos = num_cached + tok;
-    const int nb = nblk_t[t];
-    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
-    const uint32_t s_addr = tmem + lane_base + t * 128;
-    const uint32_t o_addr = tmem + lane_base + TcCfg::kOCol + t * 128;
-    const uint32_t p_row = smem_u32(smem + TcCfg::kPOff + t * TcCfg::kQBytes) + r * 128;
-    const uint32_t r7 = static_cast<uint32_t>(r & 7);
-    const float ninf = -INFINITY;
-    const float2 sc2 = make_float2(a.scale_log2, a.scale_log2);
-    float m = ninf, l = 0.f;
-    bool ok = true;
-    for (int j = 0; j < nb; ++j) {
-      ok = __all_sync(0xffffffffu, mbar_wait_fast(&s_full[t], j & 1, abort_flag));
-      if (!ok) break;
-      tc_fence_after();
-      const int k0 = key_lo + j * TcCfg::kBlockKeys;
-      const bool need_mask =
-          (k0 + TcCfg::kBlockKeys - 1 > qpos) || (k0 + TcCfg::kBlockKeys > key_end);
-      const bool warp_masks = __any_sync(0xffffffffu, need_mask);
-      // Row max over all 128 scores; then the exponentials of the first 64 from registers, and of
-      // the last 64 from a second read of TMEM (holding all 128 scores and 64 packed P words at
-      // once does not fit the register budget).  S_t is released after that second read.
-      float mx;
-      float2 suma[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) suma[i] = make_float2(0.f, 0.f);
-      uint32_t pk[4][16];
-      float alpha = 1.f;
-      bool rescale = false;
-      {
-        float s0[32], s1[32];
-        {
-          float s2[32], s3[32];
-          tmem_ld32(s_addr, s0);
-          tmem_ld32(s_addr + 32, s1);
-          tmem_ld32(s_addr + 64, s2);
-          tmem_ld32(s_addr + 96, s3);
-          tmem_wait_ld();
-          if (need_mask) {
-            mask_scores32(s0, k0, qpos, key_end);
-            mask_scores32(s1, k0 + 32, qpos, key_end);
-            mask_scores32(s2, k0 + 64, qpos, key_end);
-            mask_scores32(s3, k0 + 96, qpos, key_end);
+      // No copy may still be landing when the CTA exits: wait for the last use of each slot.
+      if (lane == 0) {
+        for (int p = issued > NS ? issued - NS : 0; p < issued; ++p) {
+          if (!mbar_wait(&slot_full[p % NS], (p / NS) & 1)) {
+            atomicOr(&g_status_word, kErrTimeout);
+            break;
           }
-          mx = max128(s0, s1, s2, s3) * a.scale_log2;
         }
-        // The running max m only moves (and O is rescaled) when the block's max exceeds it by
-        // more than 2^8.
-        if (mx > m + 8.f) {
-          alpha = fast_exp2(m - mx);
-          rescale = j > 0;
-          m = mx;
-        }
-        const float neg_mu = m == ninf ? 0.f : -m;
-        const float2 nm2 = make_float2(neg_mu, neg_mu);
-        if (warp_masks) {
-          exp_pack32<true>(s0, sc2, nm2, suma, pk[0]);
-          exp_pack32<true>(s1, sc2, nm2, suma, pk[1]);
-        } else {
-          exp_pack32<false>(s0, sc2, nm2, suma, pk[0]);
-          exp_pack32<false>(s1, sc2, nm2, suma, pk[1]);
-        }
-        pin16(pk[0]);
-        pin16(pk[1]);
       }
-      {
-        float s2[32], s3[32];
-        tmem_ld32(s_addr + 64, s2);
-        tmem_ld32(s_addr + 96, s3);
-        tmem_wait_ld();
+    } else if (warp == 9 || warp == 10) {
+      if (warp == 9) {
+        tmem_alloc(tmem_holder, TcCfg::kTmemCols);
+        tmem_relinquish();
         tc_fence_before();
-        mbar_arrive(&s_free[t]);  // the MMA may now overwrite S_t with S_t(j + 1)
-        const float neg_mu = m == ninf ? 0.f : -m;
-        const float2 nm2 = make_float2(neg_mu, neg_mu);
-        if (warp_masks) {
-          if (need_mask) {
-            mask_scores32(s2, k0 + 64, qpos, key_end);
-            mask_scores32(s3, k0 + 96, qpos, key_end);
+        if (lane == 0) mbar_arrive(tmem_ready);
+      }
+      if (wait_tmem()) {
+        // ---------------- MMA issuers: warp 9 issues every S = Q K^T, warp 10 every O += P V ------
+        // Two issuing threads, two independent MMA streams (different TMEM columns and operands): the
+        // issue queue of one thread is shallow, so any wait in a single issuer would leave the tensor
+        // core idle; with two, one stream keeps it busy while the other waits.  tcgen05.commit tracks
+        // the MMAs of the committing thread only, so each stream signals its own barriers.
+        if (lane == 0) {
+          const bool is_pv = warp == 10;
+          constexpr uint32_t kIdescS = umma_idesc_bf16(128, 128, false);
+          constexpr uint32_t kIdescPV = umma_idesc_bf16(128, 128, true);
+          const uint32_t ring = smem_u32(smem + TcCfg::kRingOff);
+          bool ok = true;
+          auto wait_slot = [&](int p) -> bool {
+            return mbar_wait_mma(&slot_full[p % NS], (p / NS) & 1, abort_flag);
+          };
+          // Descriptors are built once; operand offsets are added to their start-address field
+          // (shared-memory addresses >> 4 fit its 14 bits with room to spare).
+          const uint64_t dq = umma_smem_desc_sw128(smem_u32(smem + TcCfg::kQOff), 16, 1024);
+          const uint64_t dp = umma_smem_desc_sw128(smem_u32(smem + TcCfg::kPOff), 16, 1024);
+          const uint64_t dk = umma_smem_desc_sw128(ring, 16, 1024);
+          const uint64_t dv = umma_smem_desc_sw128(ring, 2048, 1024);  // [page][half][16 keys][64]
+          constexpr uint32_t kSlot16 = TcCfg::kSlotBytes >> 4;
+          if (!is_pv) {
+            // S_t(j) = Q_t K_j^T into tile t's S columns, as soon as tile t holds S_t(j-1) in
+            // registers and K_j has landed (and, for S(0), Q is stored).  The tiles are not coupled:
+            // each goes as soon as its own softmax has released its S columns.
+            ok = nblk == 0 || mbar_wait_mma(q_ready, 0, abort_flag);
+            for (int j = 0; ok && j < nblk; ++j) {
+              if (!(ok = wait_slot(pos_k(j)))) break;
+              const uint64_t kd = dk + (pos_k(j) % NS) * kSlot16;
+              for (int t = 0; ok && t < 2; ++t) {
+                if (j < nblk_t[t]) {
+                  if (j > 0 && !(ok = mbar_wait_mma(&s_free[t], (j - 1) & 1, abort_flag))) break;
+                  tc_fence_after();
+                  const uint64_t qd = dq + t * (TcCfg::kQBytes >> 4);
+#pragma unroll
+                  for (int kk = 0; kk < 8; ++kk) {
+                    const uint32_t off = ((kk >> 2) * 16384 + (kk & 3) * 32) >> 4;
+                    umma_bf16_ss(tmem + t * 128, qd + off, kd + off, kIdescS, kk > 0 ? 1u : 0u);
+                  }
+                  umma_commit(&s_full[t]);
+                }
+              }
+              if (!ok) break;
+              umma_commit(&slot_empty[pos_k(j) % NS]);
+            }
+          } else {
+            // O_t += P_t(j) V_j once tile t's P(j) is stored and V_j has landed.
+            for (int j = 0; ok && j < nblk; ++j) {
+              if (!(ok = wait_slot(pos_v(j)))) break;
+              const uint64_t vd = dv + (pos_v(j) % NS) * kSlot16;
+              for (int t = 0; ok && t < 2; ++t) {
+                if (j < nblk_t[t]) {
+                  if (!(ok = mbar_wait_mma(&p_full[t], j & 1, abort_flag))) break;
+                  tc_fence_after();
+#pragma unroll
+                  for (int kk = 0; kk < 8; ++kk)
+                    umma_bf16_ss(tmem + TcCfg::kOCol + t * 128,
+                                 dp + t * (TcCfg::kQBytes >> 4) +
+                                     (((kk >> 2) * 16384 + (kk & 3) * 32) >> 4),
+                                 vd + kk * (kPageBytes >> 4), kIdescPV, (j > 0 || kk > 0) ? 1u : 0u);
+                  umma_commit(&pv_done[t]);
+                }
+              }
+              if (!ok) break;
+              umma_commit(&slot_empty[pos_v(j) % NS]);
+            }
           }
-          exp_pack32<true>(s2, sc2, nm2, suma, pk[2]);
-          exp_pack32<true>(s3, sc2, nm2, suma, pk[3]);
-        } else {
-          exp_pack32<false>(s2, sc2, nm2, suma, pk[2]);
-          exp_pack32<false>(s3, sc2, nm2, suma, pk[3]);
+          if (!ok) {
+            atomicOr(&g_status_word, kErrTimeout);
+            *abort_flag = 1;
+          }
+          // Every MMA issued so far (by both issuers) must finish before TMEM is freed or the CTA
+          // exits: each issuer commits once to mma_drain (two arrivals complete it).
+          umma_commit(mma_drain);
+          if (!mbar_wait(mma_drain, 0)) atomicOr(&g_status_word, kErrTimeout);
         }
+        __syncwarp();
       }
-      const float2 s01 = __fadd2_rn(suma[0], suma[1]);
-      const float2 s23 = __fadd2_rn(suma[2], suma[3]);
-      const float2 st = __fadd2_rn(s01, s23);
-      l = l * alpha + (st.x + st.y);
-
-      // This tile's previous P*V must be complete before its P buffer is overwritten and before
-      // O is rescaled.  It is waited on every block, in order, so a parity wait is never
-      // satisfied by an older phase; it was issued a whole block ago, so the wait is normally free.
-      if (j > 0) {
-        ok = __all_sync(0xffffffffu, mbar_wait_fast(&pv_done[t], (j - 1) & 1, abort_flag));
-        if (!ok) break;
-        tc_fence_after();
-      }
-      const bool any_rescale = __any_sync(0xffffffffu, rescale);
-      if (j > 0 && any_rescale) {
-        const float f = rescale ? alpha : 1.f;
-        for (int c = 0; c < 16; ++c) {
-          float ov[8];
-          tmem_ld8(o_addr + c * 8, ov);
-          tmem_wait_ld();
+    }
+  } else {
+    setmaxnreg_inc<TcCfg::kSoftmaxRegs>();
+      // Q tiles into the swizzled K-major layout: 256 rows (2 tiles x 64 tokens x 2 heads) of 16
+      // chunks of 16 bytes; each load instruction of a warp covers two whole rows (512 contiguous
+      // bytes: one token's two heads), so the loads coalesce.  All 16 loads are issued before any
+      // store (a shared store between them would make each load wait for the previous one).
+      uint4 v[16];
 #pragma unroll
-          for (int i = 0; i < 8; ++i) ov[i] *= f;
-          tmem_st8(o_addr + c * 8, ov);
-        }
-        tmem_wait_st();
+      for (int i = 0; i < 16; ++i) {
+        const int f = i * 256 + threadIdx.x;
+        const int t = f >> 11, r = (f >> 4) & 127, u = f & 15;
+        const bool valid = (r >> 1) < (t == 0 ? n_a : n_b);
+        const int tok = (t == 0 ? tok_a : tok_b) + (r >> 1);
+        const __nv_bfloat16* src = a.q + static_cast<long long>(flat_start + tok) * a.q_row_stride +
+                                   (kvh * kGroup + (r & 1)) * kHeadDim + u * 8;
+        v[i] = valid ? __ldg(reinterpret_cast<const uint4*>(src)) : make_uint4(0u, 0u, 0u, 0u);
       }
 #pragma unroll
-      for (int u = 0; u < 16; ++u) {
-        const int c = u >> 2, i = (u & 3) * 4;
-        st_shared_v4(p_row + (u >> 3) * 16384 + (((u & 7) ^ r7) << 4), pk[c][i], pk[c][i + 1],
-                     pk[c][i + 2], pk[c][i + 3]);
+      for (int i = 0; i < 16; ++i) {
+        const int f = i * 256 + threadIdx.x;
+        const int t = f >> 11, r = (f >> 4) & 127, u = f & 15;
+        st_shared_v4(smem_u32(smem + TcCfg::kQOff + t * TcCfg::kQBytes) + tile128_off(r, u), v[i].x,
+                     v[i].y, v[i].z, v[i].w);
       }
       fence_proxy_async_smem();
-      tc_fence_before();
-      mbar_arrive(&p_full[t]);
-    }
-    if (!ok) {
-      if (lane == 0) {
-        atomicOr(&g_status_word, kErrTimeout);
-        *abort_flag = 1;
-      }
-    } else if (nb > 0) {
-      // This tile's last P*V (the phase before it was waited on in the last block).
-      ok = __all_sync(0xffffffffu, mbar_wait_fast(&pv_done[t], (nb - 1) & 1, abort_flag));
-      if (!ok && lane == 0) {
-        atomicOr(&g_status_word, kErrTimeout);
-        *abort_flag = 1;
-      }
-    }
-    if (ok) {
-      tc_fence_after();
-      const float inv = l > 0.f ? 1.f / l : 0.f;
-      const int head = kvh * kGroup + (r & 1);
-      // Row inside the item's partial rows (split items have adjacent tiles: token order).
-      const int prow_r = t * 128 + r;
+      mbar_arrive(q_ready);
+    if (wait_tmem()) {
+        // ---------------- softmax warpgroups: thread = row of tile t ----------------
+        const int t = warp >> 2;
+        const int r = threadIdx.x & 127;
+        const bool valid = (r >> 1) < (t == 0 ? n_a : n_b);
+        const int tok = (t == 0 ? tok_a : tok_b) + (r >> 1);
+        const int qpos = num_cached + tok;
+        const int nb = nblk_t[t];
+        const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+        const uint32_t s_addr = tmem + lane_base + t * 128;
+        const uint32_t o_addr = tmem + lane_base + TcCfg::kOCol + t * 128;
+        const uint32_t p_row = smem_u32(smem + TcCfg::kPOff + t * TcCfg::kQBytes) + r * 128;
+        const uint32_t r7 = static_cast<uint32_t>(r & 7);
+        const float ninf = -INFINITY;
+        const float2 sc2 = make_float2(a.scale_log2, a.scale_log2);
+        float m = ninf, l = 0.f;
+        bool ok = true;
+        for (int j = 0; j < nb; ++j) {
+          ok = __all_sync(0xffffffffu, mbar_wait_fast(&s_full[t], j & 1, abort_flag));
+          if (!ok) break;
+          tc_fence_after();
+          const int k0 = key_lo + j * TcCfg::kBlockKeys;
+          const bool need_mask =
+              (k0 + TcCfg::kBlockKeys - 1 > qpos) || (k0 + TcCfg::kBlockKeys > key_end);
+          const bool warp_masks = __any_sync(0xffffffffu, need_mask);
+          // All 128 scores of the row come out of TMEM in one read, after which S_t is released at
+          // once: the MMA computes S_t(j + 1) while this block's max, exponentials and P run.
+          float2 suma[4];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        float ov[32];
-        if (nb > 0) {
-          tmem_ld32(o_addr + c * 32, ov);
-          tmem_wait_ld();
-        } else {
+          for (int i = 0; i < 4; ++i) suma[i] = make_float2(0.f, 0.f);
+          uint32_t pk[4][16];
+          float alpha = 1.f;
+          bool rescale = false;
+          {
+            float s0[32], s1[32], s2[32], s3[32];
+            tmem_ld32(s_addr, s0);
+            tmem_ld32(s_addr + 32, s1);
+            tmem_ld32(s_addr + 64, s2);
+            tmem_ld32(s_addr + 96, s3);
+            tmem_wait_ld();
+            tc_fence_before();
+            mbar_arrive(&s_free[t]);  // the MMA may now overwrite S_t with S_t(j + 1)
+            if (need_mask) {
+              mask_scores32(s0, k0, qpos, key_end);
+              mask_scores32(s1, k0 + 32, qpos, key_end);
+              mask_scores32(s2, k0 + 64, qpos, key_end);
+              mask_scores32(s3, k0 + 96, qpos, key_end);
+            }
+            const float mx = max128(s0, s1, s2, s3) * a.scale_log2;
+            // The running max m only moves (and O is rescaled) when the block's max exceeds it by
+            // more than 2^8.
+            if (mx > m + 8.f) {
+              alpha = fast_exp2(m - mx);
+              rescale = j > 0;
+              m = mx;
+            }
+            const float neg_mu = m == ninf ? 0.f : -m;
+            const float2 nm2 = make_float2(neg_mu, neg_mu);
+            if (warp_masks) {
+              exp_pack32<true>(s0, sc2, nm2, suma, pk[0]);
+              exp_pack32<true>(s1, sc2, nm2, suma, pk[1]);
+              exp_pack32<true>(s2, sc2, nm2, suma, pk[2]);
+              exp_pack32<true>(s3, sc2, nm2, suma, pk[3]);
+            } else {
+              exp_pack32<false>(s0, sc2, nm2, suma, pk[0]);
+              exp_pack32<false>(s1, sc2, nm2, suma, pk[1]);
+              exp_pack32<false>(s2, sc2, nm2, suma, pk[2]);
+              exp_pack32<false>(s3, sc2, nm2, suma, pk[3]);
+            }
+          }
+          const float2 s01 = __fadd2_rn(suma[0], suma[1]);
+          const float2 s23 = __fadd2_rn(suma[2], suma[3]);
+          const float2 st = __fadd2_rn(s01, s23);
+          l = l * alpha + (st.x + st.y);
+
+          // This tile's previous P*V must be complete before its P buffer is overwritten and before
+          // O is rescaled.  It is waited on every block, in order, so a parity wait is never
+          // satisfied by an older phase; it was issued a whole block ago, so the wait is normally free.
+          if (j > 0) {
+            ok = __all_sync(0xffffffffu, mbar_wait_fast(&pv_done[t], (j - 1) & 1, abort_flag));
+            if (!ok) break;
+            tc_fence_after();
+          }
+          const bool any_rescale = __any_sync(0xffffffffu, rescale);
+          if (j > 0 && any_rescale) {
+            const float f = rescale ? alpha : 1.f;
+            for (int c = 0; c < 16; ++c) {
+              float ov[8];
+              tmem_ld8(o_addr + c * 8, ov);
+              tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) ov[i] = 0.f;
+              for (int i = 0; i < 8; ++i) ov[i] *= f;
+              tmem_st8(o_addr + c * 8, ov);
+            }
+            tmem_wait_st();
+          }
+#pragma unroll
+          for (int u = 0; u < 16; ++u) {
+            const int c = u >> 2, i = (u & 3) * 4;
+            st_shared_v4(p_row + (u >> 3) * 16384 + (((u & 7) ^ r7) << 4), pk[c][i], pk[c][i + 1],
+                         pk[c][i + 2], pk[c][i + 3]);
+          }
+          fence_proxy_async_smem();
+          tc_fence_before();
+          mbar_arrive(&p_full[t]);
         }
-        if (valid) {
-          if (part_row < 0) {
-            __nv_bfloat16* dst = a.out +
-                                 static_cast<long long>(flat_start + tok) * a.out_row_stride +
-                                 head * kHeadDim + c * 32;
-#pragma unroll
-            for (int u = 0; u < 4; ++u)
-              reinterpret_cast<uint4*>(dst)[u] =
-                  make_uint4(pack_bf16(ov[8 * u] * inv, ov[8 * u + 1] * inv),
-                             pack_bf16(ov[8 * u + 2] * inv, ov[8 * u + 3] * inv),
-                             pack_bf16(ov[8 * u + 4] * inv, ov[8 * u + 5] * inv),
-                             pack_bf16(ov[8 * u + 6] * inv, ov[8 * u + 7] * inv));
-          } else {
-            const long long prow = static_cast<long long>(part_row + prow_r) * a.num_kv + kvh;
-            float* dst = a.ws_o + prow * kHeadDim + c * 32;
-#pragma unroll
-            for (int u = 0; u < 8; ++u)
-              reinterpret_cast<float4*>(dst)[u] = make_float4(
-                  ov[4 * u] * inv, ov[4 * u + 1] * inv, ov[4 * u + 2] * inv, ov[4 * u + 3] * inv);
-            if (c == 0) a.ws_lse[prow] = l > 0.f ? m + __log2f(l) : -INFINITY;
+        if (!ok) {
+          if (lane == 0) {
+            atomicOr(&g_status_word, kErrTimeout);
+            *abort_flag = 1;
+          }
+        } else if (nb > 0) {
+          // This tile's last P*V (the phase before it was waited on in the last block).
+          ok = __all_sync(0xffffffffu, mbar_wait_fast(&pv_done[t], (nb - 1) & 1, abort_flag));
+          if (!ok && lane == 0) {
+            atomicOr(&g_status_word, kErrTimeout);
+            *abort_flag = 1;
           }
         }
-      }
+        if (ok) {
+          tc_fence_after();
+          const float inv = l > 0.f ? 1.f / l : 0.f;
+          const int head = kvh * kGroup + (r & 1);
+          // Row inside the item's partial rows (split items have adjacent tiles: token order).
+          const int prow_r = t * 128 + r;
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            float ov[32];
+            if (nb > 0) {
+              tmem_ld32(o_addr + c * 32, ov);
+              tmem_wait_ld();
+            } else {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) ov[i] = 0.f;
+            }
+            if (valid) {
+              if (part_row < 0) {
+                __nv_bfloat16* dst = a.out +
+                                     static_cast<long long>(flat_start + tok) * a.out_row_stride +
+                                     head * kHeadDim + c * 32;
+#pragma unroll
+                for (int u = 0; u < 4; ++u)
+                  reinterpret_cast<uint4*>(dst)[u] =
+                      make_uint4(pack_bf16(ov[8 * u] * inv, ov[8 * u + 1] * inv),
+                                 pack_bf16(ov[8 * u + 2] * inv, ov[8 * u + 3] * inv),
+                                 pack_bf16(ov[8 * u + 4] * inv, ov[8 * u + 5] * inv),
+                                 pack_bf16(ov[8 * u + 6] * inv, ov[8 * u + 7] * inv));
+              } else {
+                const long long prow = static_cast<long long>(part_row + prow_r) * a.num_kv + kvh;
+                float* dst = a.ws_o + prow * kHeadDim + c * 32;
+#pragma unroll
+                for (int u = 0; u < 8; ++u)
+                  reinterpret_cast<float4*>(dst)[u] = make_float4(
+                      ov[4 * u] * inv, ov[4 * u + 1] * inv, ov[4 * u + 2] * inv, ov[4 * u + 3] * inv);
+                if (c == 0) a.ws_lse[prow] = l > 0.f ? m + __log2f(l) : -INFINITY;
+              }
+            }
+          }
+        }
     }
   }
 

@@ -26,3 +26,21 @@ def cuda_device():
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
     return torch.device("cuda:0")
+
+
+@pytest.fixture(autouse=True)
+def _device_status_clean(request: pytest.FixtureRequest):
+    """After every GPU test: no kernel may have left a status bit set (a bounded wait that gave
+    up, an out-of-range slot, block or position).  Tests that plant such a fault read and clear
+    the word themselves."""
+    yield
+    if request.node.get_closest_marker("gpu") is None:
+        return
+    import torch
+
+    if not torch.cuda.is_available():
+        return
+    from miniserve_b200 import _capi
+
+    status = _capi.device_status(int(torch.cuda.current_stream().cuda_stream))
+    assert status == 0, f"a kernel left device status bits {status:#x} set during this test"
