@@ -61,12 +61,13 @@ def parse() -> argparse.Namespace:
                    help="layers per step (28 for the headline; fewer only for small profiles)")
     p.add_argument("--tokens", type=int, default=4096,
                    help="--workload qkv: tokens per step")
-    p.add_argument("--workload", choices=["cfg1", "cfg2", "cfg3", "cfg4", "cfg5", "qkv"],
+    p.add_argument("--workload", choices=["cfg1", "cfg2", "cfg3", "cfg4", "cfg5", "qkv", "prefill"],
                    default="cfg2",
                    help="cfg2 is the headline; cfg1 (8 short decode rows), cfg3 (mixed prefill), "
                         "cfg4 (prefix + verify) and cfg5 (box scale: 8192 rows sharded over the "
                         "ranks) alone; qkv times kernel E (qkv projection + norm/RoPE/scatter) "
-                        "beside cuBLAS + kernel A at --tokens tokens")
+                        "beside cuBLAS + kernel A at --tokens tokens; prefill times the tensor-core "
+                        "kernel alone on config 3's chunks and on fresh prompts")
     p.add_argument("--no-extras", action="store_true",
                    help="headline only: skip the config 3 / 4 / 5 keys")
     p.add_argument("--no-qkv-part", action="store_true",
@@ -481,6 +482,75 @@ def run_qkv_only(args: argparse.Namespace, rank: int, device: torch.device) -> N
                       "qkv_projection": r}), flush=True)
 
 
+def run_prefill_only(rank: int, device: torch.device) -> None:
+    """--workload prefill: the attention call alone on prefill-only batches (the tensor-core
+    kernel, plus the combine pass where a plan splits tiles): config 3's two chunks, fresh prompts
+    of 2048 / 4096 / 8192 tokens and 1024 new tokens over 8192 cached.  CUDA-graph replay of 10
+    calls, best of 5 replays; causal FLOPs against the measured bf16 peak."""
+    from miniserve_b200 import _capi
+    from miniserve_b200.attention import attend, build_attention_metadata
+    from miniserve_b200.kv_pool import allocate_kv_cache
+    from miniserve_b200.workloads import config3, custom
+
+    if rank != 0:
+        return
+    pk, src = peaks()
+    burst = float(pk["bf16_tflops"])
+    sustained = float(pk.get("bf16_tflops_sustained", burst))
+    cases = {
+        "config3_chunks": [c for c in config3(seed=SEED).chunks if c.num_new > 64],
+        "fresh_2048": custom([(2048, 0)], seed=1).chunks,
+        "fresh_4096": custom([(4096, 0)], seed=1).chunks,
+        "fresh_8192": custom([(8192, 0)], seed=1).chunks,
+        "1024_over_8192": custom([(1024, 8192)], seed=1).chunks,
+    }
+    stream = torch.cuda.current_stream(device)
+    res = {}
+    for name, chunks in cases.items():
+        nb = max(b for c in chunks for b in c.block_table) + 1
+        t = max(c.flat_start + c.num_new for c in chunks)
+        g = torch.Generator(device=device).manual_seed(3)
+        pool, views = allocate_kv_cache(1, nb, KVH, device, zero=False)
+        pool.normal_(generator=g)
+        kc, vc = views[0]
+        q = torch.randn(t, H, D, generator=g, device=device).bfloat16()
+        out = torch.empty_like(q)
+        meta = build_attention_metadata(chunks, torch.zeros(t, dtype=torch.int64, device=device), 16)
+        attend(q, kc, vc, meta, D**-0.5, out=out)
+        torch.cuda.synchronize(device)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for _ in range(10):
+                attend(q, kc, vc, meta, D**-0.5, out=out)
+        graph.replay()
+        torch.cuda.synchronize(device)
+        best = float("inf")
+        for _ in range(5):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            graph.replay()
+            e1.record(stream)
+            torch.cuda.synchronize(device)
+            best = min(best, e0.elapsed_time(e1) * 1e3 / 10)
+        del graph
+        status = _capi.device_status(int(stream.cuda_stream))
+        if status:
+            raise RuntimeError(f"device status {status:#x} ({name})")
+        pairs = sum(c.num_new * c.num_cached + c.num_new * (c.num_new + 1) // 2 for c in chunks)
+        tflops = 4 * D * H * pairs / (best * 1e-6) / 1e12
+        res[name] = {"us": round(best, 2), "TFLOPS_causal": round(tflops, 1),
+                     "frac_of_burst": round(tflops / burst, 3),
+                     "frac_of_sustained": round(tflops / sustained, 3),
+                     "tc_items": int(meta.info.n_tc_items), "combine": int(meta.info.n_combine)}
+    head = res["config3_chunks"]
+    print(json.dumps({"metric": "prefill attention TFLOP/s (tensor-core kernel, config 3's chunks)",
+                      "value": head["TFLOPS_causal"], "unit": "TFLOP/s", "higher_is_better": True,
+                      "n_gpus": 1, "dtype": "bf16", "data": "synthetic",
+                      "config": {"workload": "prefill-only attention calls"},
+                      "peak_source": src, "cases": res,
+                      "timing": "CUDA-graph replay of 10 calls, best of 5, per call"}), flush=True)
+
+
 def run_e2e(ws: DeviceStep, args: argparse.Namespace, world: int) -> tuple[float, int, int]:
     """The same step through the public Python API with host buffers: each step prepares its
     positions and slot mapping from the block tables (ms_prepare_step), plans (ms_plan_build)
@@ -866,8 +936,11 @@ def main() -> None:
     if world > 1:
         torch.distributed.barrier()
 
-    if args.workload == "qkv":
-        run_qkv_only(args, rank, device)
+    if args.workload in ("qkv", "prefill"):
+        if args.workload == "qkv":
+            run_qkv_only(args, rank, device)
+        else:
+            run_prefill_only(rank, device)
         if world > 1:
             torch.distributed.barrier()
             torch.distributed.destroy_process_group()
