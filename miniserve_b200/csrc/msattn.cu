@@ -155,6 +155,27 @@ static cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, unsigned block, s
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
+// The same, as clusters of two CTAs (consecutive blockIdx.x) that share distributed shared memory.
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_pairs(void (*kernel)(KArgs...), dim3 grid, unsigned block, size_t smem,
+                                cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = 2;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 // ---- attention launch configurations --------------------------------------------------------
 
 constexpr int kDecodeWarps = 4, kDecodeStages = 8;
@@ -218,6 +239,10 @@ static int ensure_smem_attrs() {
   e = cudaFuncSetAttribute(ms::qkv_proj_norm_rope_kernel<2>,
                            cudaFuncAttributeMaxDynamicSharedMemorySize, ms::QkvCfg<2>::kSmemBytes);
   if (e != cudaSuccess) return cuda_fail("cudaFuncSetAttribute(qkv 2)", e);
+  e = cudaFuncSetAttribute(ms::qkv_proj_norm_rope_kernel<1, 2>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           ms::QkvCfg<1, 2>::kSmemBytes);
+  if (e != cudaSuccess) return cuda_fail("cudaFuncSetAttribute(qkv split-K)", e);
   done[dev] = true;
   return MS_OK;
 }
@@ -496,13 +521,20 @@ extern "C" int ms_qkv_proj_norm_rope_scatter(
   const bool pairs = num_heads % 2 == 0 && num_kv_heads % 2 == 0 &&
                      2 * m_tiles * (rows / 2) >= static_cast<int64_t>(sms);
   qa.num_tiles = static_cast<int>(m_tiles * (pairs ? rows / 2 : rows));
-  const int grid = qa.num_tiles < sms ? qa.num_tiles : sms;  // persistent: one CTA per SM
+  // Few one-head tiles (decode-sized steps: up to 2 x 128 tokens for 32 head rows on 148 SMs):
+  // each tile runs on a pair of CTAs that split the hidden dimension, so every CTA streams half
+  // the operands and stages half the rows.
+  const bool split = !pairs && (hidden / 64) % 2 == 0 && 2 * qa.num_tiles <= sms;
+  const int grid = split ? 2 * qa.num_tiles
+                         : (qa.num_tiles < sms ? qa.num_tiles : sms);  // persistent: one CTA/SM
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
   const cudaError_t e =
-      pairs ? launch(ms::qkv_proj_norm_rope_kernel<2>, grid, ms::QkvCfg<2>::kThreads,
-                     ms::QkvCfg<2>::kSmemBytes, s, xmap, wmap, qa, st)
-            : launch(ms::qkv_proj_norm_rope_kernel<1>, grid, ms::QkvCfg<1>::kThreads,
-                     ms::QkvCfg<1>::kSmemBytes, s, xmap, wmap, qa, st);
+      pairs   ? launch(ms::qkv_proj_norm_rope_kernel<2>, grid, ms::QkvCfg<2>::kThreads,
+                       ms::QkvCfg<2>::kSmemBytes, s, xmap, wmap, qa, st)
+      : split ? launch_pairs(ms::qkv_proj_norm_rope_kernel<1, 2>, grid, ms::QkvCfg<1, 2>::kThreads,
+                             ms::QkvCfg<1, 2>::kSmemBytes, s, xmap, wmap, qa, st)
+              : launch(ms::qkv_proj_norm_rope_kernel<1>, grid, ms::QkvCfg<1>::kThreads,
+                       ms::QkvCfg<1>::kSmemBytes, s, xmap, wmap, qa, st);
   if (e != cudaSuccess) return cuda_fail("qkv_proj_norm_rope launch", e);
   return MS_OK;
 }

@@ -8,10 +8,12 @@ Two kinds of inputs:
     projection is exact and any accumulation order gives the same bf16 output.  There kernel E
     must equal torch.matmul (cuBLAS) + kernel A bit for bit: q, the K rows and the V rows, and no
     pool slot outside slot_mapping may change.
-  * "gaussian": ordinary random inputs.  The GEMM's accumulation order can move a projection
-    output by one bf16 ulp, which RMSNorm and RoPE carry into the head's outputs; the tolerance
-    is stated in the test (at most 2 bf16 ulps anywhere, and 99.9 % of values within 1 ulp), and
-    the fp32 CPU restatement of the whole op bounds both paths.
+  * "gaussian": ordinary random inputs.  The GEMM's accumulation order (kernel E's tcgen05
+    tiles, split-K pairs for small steps, against cuBLAS) moves a few projection outputs by a
+    bf16 ulp and, where the fp32 sum cancels, by more; RMSNorm and RoPE carry that into q and k.
+    Bounds: every element within the order tolerance derived in `_order_tolerance`, 99.9 % of
+    elements within one bf16 ulp, and both paths within a fixed distance of the fp32 CPU
+    restatement of the whole op.
 """
 
 from __future__ import annotations
@@ -46,6 +48,52 @@ def _inputs(t: int, kind: str, seed: int, num_blocks: int, max_pos: int = 4096):
     return x.bfloat16(), w.bfloat16(), qw.bfloat16(), kw.bfloat16(), positions, slots
 
 
+def _bf16_spacing(m: torch.Tensor) -> torch.Tensor:
+    """The spacing of bf16 numbers at magnitude m: 2^(floor(log2 m) - 7)."""
+    m = m.abs().clamp_min(2.0**-126)
+    return torch.exp2(torch.floor(torch.log2(m)) - 7)
+
+
+def _order_tolerance(x, w, qw, kw, positions, outs_a, outs_b):
+    """Per-element bound on |a - b| between two implementations of the op that differ only in
+    the projection's fp32 accumulation order (float64 tensors, [T, heads, D] for q, k, v).
+
+    Two terms.  (1) The accumulation: any fp32 order of a K-term dot product of bf16 values is
+    within K * 2^-24 * sum|x_i w_i| of the exact sum (K = 1024: 2^-14), tensor-core rounding
+    included with a factor 2, and two orders are within twice that: 2^-12 * sum|x_i w_i|.  RMSNorm
+    scales that error by rsqrt(mean p^2) * |weight|; RoPE combines two such errors with |cos| and
+    |sin|.  (2) The rounding chain: a projection that moved by one ulp can flip the bf16 rounding
+    of the norm (two roundings) and of RoPE's products and sum (layers.py:18-22, 56-65): 4 ulps
+    at the largest operand of the last rounding (for RoPE the larger product; where the products
+    cancel, that is far above the result's own spacing).  On the oracle itself, orders from 1 to
+    1024 partial sums stay within 0.83 of this bound at 64 to 4096 tokens."""
+    t = x.shape[0]
+    xd, wd = x.double(), w.double()
+    p = xd @ wd.t()
+    err = 2.0**-12 * (xd.abs() @ wd.abs().t())
+    cos_t, sin_t = orc.rope_tables(D, 4096, THETA)
+    c = cos_t[positions].unsqueeze(1).double()
+    sn = sin_t[positions].unsqueeze(1).double()
+    sizes = [H * D, KVH * D, KVH * D]
+    ps, es = p.split(sizes, dim=-1), err.split(sizes, dim=-1)
+    bounds = []
+    for i, (nh, wt) in enumerate(((H, qw), (KVH, kw))):
+        pp, ee = ps[i].reshape(t, nh, D), es[i].reshape(t, nh, D)
+        inv = torch.rsqrt(pp.pow(2).mean(-1, keepdim=True) + EPS)
+        n = pp * inv * wt.double()
+        en = ee * inv * wt.double().abs()
+        lo, hi = n.chunk(2, dim=-1)
+        rot = torch.cat((-hi, lo), dim=-1)
+        elo, ehi = en.chunk(2, dim=-1)
+        erot = torch.cat((ehi, elo), dim=-1)
+        scale = torch.maximum(torch.maximum((n * c).abs(), (rot * sn).abs()),
+                              torch.maximum(outs_a[i].abs(), outs_b[i].abs()))
+        bounds.append(4 * _bf16_spacing(scale) + en * c.abs() + erot * sn.abs())
+    v_scale = torch.maximum(outs_a[2].abs(), outs_b[2].abs())
+    bounds.append(4 * _bf16_spacing(v_scale) + es[2].reshape(t, KVH, D))
+    return bounds
+
+
 def _run(path: str, x, w, qw, kw, positions, slots, num_blocks: int, device, positions_mode=False):
     cos_t, sin_t = orc.rope_tables(D, 4096, THETA)
     pool, views = allocate_kv_cache(1, num_blocks, KVH, device)
@@ -75,9 +123,10 @@ def _run(path: str, x, w, qw, kw, positions, slots, num_blocks: int, device, pos
     return q, layer_as_slots(k_cache), layer_as_slots(v_cache), status
 
 
-# 1, 77, 128 and 300 tokens run the one-head-per-tile form; 1024, 2400 and 4096 the
-# two-heads-per-tile form (2400 leaves a ragged last token block).
-@pytest.mark.parametrize("t", [1, 77, 128, 300, 1024, 2400, 4096])
+# 1, 77, 128 and 256 tokens run the split-K pairs (one-head tiles, two CTAs per tile), 300 the
+# one-head-per-tile form; 1024, 2400 and 4096 the two-heads-per-tile form (2400 leaves a ragged
+# last token block).
+@pytest.mark.parametrize("t", [1, 77, 128, 256, 300, 1024, 2400, 4096])
 def test_exact_inputs_bit_equal_to_cublas_plus_kernel_a(t: int, cuda_device) -> None:
     nb = (t + 15) // 16 + 8
     inp = _inputs(t, "exact", seed=t, num_blocks=nb)
@@ -99,10 +148,17 @@ def test_gaussian_inputs_within_stated_ulps(t: int, cuda_device) -> None:
     qb, kb, vb, sb = _run("cublas", *inp, nb, cuda_device)
     assert sa == 0 and sb == 0
     s = slots.to(cuda_device)
-    for a, b in ((qa, qb), (ka[s], kb[s]), (va[s], vb[s])):
-        ulps = bf16_ulp_diff(a, b)
-        assert int(ulps.max()) <= 2, int(ulps.max())
-        assert (ulps <= 1).float().mean().item() >= 0.999
+    outs_a = [o.cpu().double() for o in (qa, ka[s], va[s])]
+    outs_b = [o.cpu().double() for o in (qb, kb[s], vb[s])]
+    bounds = _order_tolerance(x, w, qw, kw, positions, outs_a, outs_b)
+    for name, a, b, bound in zip("qkv", outs_a, outs_b, bounds):
+        ratio = (a - b).abs() / bound
+        worst = int(ratio.argmax())
+        assert ratio.max().item() <= 1.0, (
+            f"{name}: |a - b| / bound = {ratio.max().item():.3f} at flat index {worst}: "
+            f"{a.flatten()[worst].item()} vs {b.flatten()[worst].item()}")
+        # Almost every element sits where the order does not matter: within one bf16 ulp.
+        assert (bf16_ulp_diff(a.bfloat16(), b.bfloat16()) <= 1).float().mean().item() >= 0.999, name
     # Untouched slots stay untouched.
     mask = torch.ones(nb * 16, dtype=torch.bool, device=cuda_device)
     mask[s] = False
