@@ -94,11 +94,13 @@ __device__ __forceinline__ void tma_load_5d_plain(void* smem_dst, const CUtensor
 // reduction x = n + f with n = round(x), f in [-1/2, 1/2]: adding 1.5 * 2^23 rounds x to an integer
 // held in the low mantissa bits, so no float-to-int conversion is needed.  2^f comes from a cubic
 // whose coefficients were fitted here for minimum relative error on [-1/2, 1/2] (max 7.5e-5, far
-// below the 2^-9 spacing of the bf16 P it feeds); 2^n is added to the exponent field.  x is
-// clamped to [-126, +inf); callers pass x <= 8.
-__device__ __forceinline__ float2 exp2_fma2(float2 x) {
-  x.x = fmaxf(x.x, -126.f);
-  x.y = fmaxf(x.y, -126.f);
+// below the 2^-9 spacing of the bf16 P it feeds); 2^n is added to the exponent field.  Callers
+// pass x <= 8; below -126 (masked scores are -inf) the result is exactly 0, as ex2.approx.ftz
+// gives there.
+__device__ __forceinline__ float2 exp2_fma2(float2 xin) {
+  float2 x;
+  x.x = fmaxf(xin.x, -126.f);
+  x.y = fmaxf(xin.y, -126.f);
   const float2 shifted = __fadd2_rn(x, make_float2(12582912.f, 12582912.f));
   const float2 rounded = __fadd2_rn(shifted, make_float2(-12582912.f, -12582912.f));
   const float2 f = __ffma2_rn(rounded, make_float2(-1.f, -1.f), x);
@@ -108,16 +110,17 @@ __device__ __forceinline__ float2 exp2_fma2(float2 x) {
   p = __ffma2_rn(p, f, make_float2(0.9999280571937561f, 0.9999280571937561f));
   const int nx = __float_as_int(shifted.x) - 0x4B400000;
   const int ny = __float_as_int(shifted.y) - 0x4B400000;
-  return make_float2(__int_as_float(__float_as_int(p.x) + (nx << 23)),
-                     __int_as_float(__float_as_int(p.y) + (ny << 23)));
+  return make_float2(xin.x < -126.f ? 0.f : __int_as_float(__float_as_int(p.x) + (nx << 23)),
+                     xin.y < -126.f ? 0.f : __int_as_float(__float_as_int(p.y) + (ny << 23)));
 }
 
-__device__ __forceinline__ void mask_scores32(float (&v)[32], int k0, int qpos, int key_end) {
+// Causal / range mask of 32 consecutive keys: key i is visible iff i < lim, where lim = (the
+// row's first invisible key, min(qpos + 1, key_end)) - (the first of the 32 keys).  Within a block
+// the invisible keys of a row are a suffix, so one compare with a constant and one select per
+// score suffice.
+__device__ __forceinline__ void mask_scores32(float (&v)[32], int lim) {
 #pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    const int kp = k0 + i;
-    if (kp > qpos || kp >= key_end) v[i] = -INFINITY;
-  }
+  for (int i = 0; i < 32; ++i) v[i] = i < lim ? v[i] : -INFINITY;
 }
 
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
@@ -140,24 +143,20 @@ __device__ __forceinline__ float max128(const float (&s0)[32], const float (&s1)
 }
 
 // p = 2^(s * scale_log2 - m) for 32 scores, accumulated into the pair sums and packed as 16 bf16
-// pairs.  Elements are processed in pairs with the paired fp32 instructions.  kMasked: the block
-// holds masked (-inf) scores, so every exponential goes to the MUFU (ex2(-inf) = 0); otherwise 2 of
-// every 8 pairs go to the FMA pipe (exp2_fma2), which balances the MUFU pipe against instruction
-// issue when two softmax warps share a sub-partition (measured: 0, 2, 3, 4, 5 of 8 give 79.6,
-// 76.3, 80.2, 82.8, 86.0 us on a 4096-token prompt).  The two forms are separate instantiations:
-// choosing per element at run time doubles the cost of the loop.
-template <bool kMasked>
+// pairs.  Elements are processed in pairs with the paired fp32 instructions; 2 of every 8 pairs
+// go to the FMA pipe (exp2_fma2), which balances the MUFU pipe against instruction issue when two
+// softmax warps share a sub-partition (measured: 0, 2, 3, 4, 5 of 8 give 79.6, 76.3, 80.2, 82.8,
+// 86.0 us on a 4096-token prompt).  Masked scores (-inf) give 0 on either pipe, so blocks with and
+// without masked scores run this same code: with a separate all-MUFU form for masked blocks, a
+// warpgroup in its diagonal block and the other warpgroup in an unmasked block ran two different
+// unrolled loops side by side, and the diagonal block took ~2.3x as long.
 __device__ __forceinline__ void exp_pack32(const float (&sv)[32], float2 sc2, float2 nm2,
                                            float2 (&suma)[4], uint32_t (&packed)[16]) {
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
     const float2 x = __ffma2_rn(make_float2(sv[2 * i], sv[2 * i + 1]), sc2, nm2);
-    float2 p;
-    if constexpr (kMasked) {
-      p = make_float2(fast_exp2(x.x), fast_exp2(x.y));
-    } else {
-      p = (i & 7) < 2 ? exp2_fma2(x) : make_float2(fast_exp2(x.x), fast_exp2(x.y));
-    }
+    const float2 p =
+        (i & 7) < 2 ? exp2_fma2(x) : make_float2(fast_exp2(x.x), fast_exp2(x.y));
     suma[i & 3] = __fadd2_rn(suma[i & 3], p);
     packed[i] = pack_bf16(p.x, p.y);
   }
@@ -369,13 +368,19 @@ __global__ void __launch_bounds__(TcCfg::kThreads, 1)
               umma_commit(&slot_empty[pos_k(j) % NS]);
             }
           } else {
-            // O_t += P_t(j) V_j once tile t's P(j) is stored and V_j has landed.
+            // O_t += P_t(j) V_j once tile t's P(j) is stored and V_j has landed.  Within an entry
+            // the tiles go in the order their P becomes ready, so a tile whose softmax runs late
+            // (its diagonal block, or its epilogue beside the other tile) does not hold the other
+            // tile's P*V back.  Each tile's p_full phase is j: it takes part in entries 0 .. n - 1.
             for (int j = 0; ok && j < nblk; ++j) {
               if (!(ok = wait_slot(pos_v(j)))) break;
               const uint64_t vd = dv + (pos_v(j) % NS) * kSlot16;
-              for (int t = 0; ok && t < 2; ++t) {
-                if (j < nblk_t[t]) {
-                  if (!(ok = mbar_wait_mma(&p_full[t], j & 1, abort_flag))) break;
+              int pend = (j < nblk_t[0] ? 1 : 0) | (j < nblk_t[1] ? 2 : 0);
+              for (int i = 0; pend != 0; ++i) {
+                const int t = ((pend & 1) && mbar_test_wait(&p_full[0], j & 1))   ? 0
+                              : ((pend & 2) && mbar_test_wait(&p_full[1], j & 1)) ? 1
+                                                                                  : -1;
+                if (t >= 0) {
                   tc_fence_after();
 #pragma unroll
                   for (int kk = 0; kk < 8; ++kk)
@@ -384,6 +389,10 @@ __global__ void __launch_bounds__(TcCfg::kThreads, 1)
                                      (((kk >> 2) * 16384 + (kk & 3) * 32) >> 4),
                                  vd + kk * (kPageBytes >> 4), kIdescPV, (j > 0 || kk > 0) ? 1u : 0u);
                   umma_commit(&pv_done[t]);
+                  pend &= ~(1 << t);
+                } else if (i >= 16 * kSpinLimit || ((i & 63) == 63 && *abort_flag)) {
+                  ok = false;  // the same bound and abort check as mbar_wait_mma
+                  break;
                 }
               }
               if (!ok) break;
@@ -452,7 +461,6 @@ __global__ void __launch_bounds__(TcCfg::kThreads, 1)
           const int k0 = key_lo + j * TcCfg::kBlockKeys;
           const bool need_mask =
               (k0 + TcCfg::kBlockKeys - 1 > qpos) || (k0 + TcCfg::kBlockKeys > key_end);
-          const bool warp_masks = __any_sync(0xffffffffu, need_mask);
           // All 128 scores of the row come out of TMEM in one read, after which S_t is released at
           // once: the MMA computes S_t(j + 1) while this block's max, exponentials and P run.
           float2 suma[4];
@@ -471,10 +479,11 @@ __global__ void __launch_bounds__(TcCfg::kThreads, 1)
             tc_fence_before();
             mbar_arrive(&s_free[t]);  // the MMA may now overwrite S_t with S_t(j + 1)
             if (need_mask) {
-              mask_scores32(s0, k0, qpos, key_end);
-              mask_scores32(s1, k0 + 32, qpos, key_end);
-              mask_scores32(s2, k0 + 64, qpos, key_end);
-              mask_scores32(s3, k0 + 96, qpos, key_end);
+              const int lim = min(qpos + 1, key_end) - k0;
+              mask_scores32(s0, lim);
+              mask_scores32(s1, lim - 32);
+              mask_scores32(s2, lim - 64);
+              mask_scores32(s3, lim - 96);
             }
             const float mx = max128(s0, s1, s2, s3) * a.scale_log2;
             // The running max m only moves (and O is rescaled) when the block's max exceeds it by
@@ -486,17 +495,10 @@ __global__ void __launch_bounds__(TcCfg::kThreads, 1)
             }
             const float neg_mu = m == ninf ? 0.f : -m;
             const float2 nm2 = make_float2(neg_mu, neg_mu);
-            if (warp_masks) {
-              exp_pack32<true>(s0, sc2, nm2, suma, pk[0]);
-              exp_pack32<true>(s1, sc2, nm2, suma, pk[1]);
-              exp_pack32<true>(s2, sc2, nm2, suma, pk[2]);
-              exp_pack32<true>(s3, sc2, nm2, suma, pk[3]);
-            } else {
-              exp_pack32<false>(s0, sc2, nm2, suma, pk[0]);
-              exp_pack32<false>(s1, sc2, nm2, suma, pk[1]);
-              exp_pack32<false>(s2, sc2, nm2, suma, pk[2]);
-              exp_pack32<false>(s3, sc2, nm2, suma, pk[3]);
-            }
+            exp_pack32(s0, sc2, nm2, suma, pk[0]);
+            exp_pack32(s1, sc2, nm2, suma, pk[1]);
+            exp_pack32(s2, sc2, nm2, suma, pk[2]);
+            exp_pack32(s3, sc2, nm2, suma, pk[3]);
           }
           const float2 s01 = __fadd2_rn(suma[0], suma[1]);
           const float2 s23 = __fadd2_rn(suma[2], suma[3]);
@@ -548,42 +550,97 @@ __global__ void __launch_bounds__(TcCfg::kThreads, 1)
           }
         }
         if (ok) {
+          // Epilogue.  Thread r holds row r of O in TMEM; the rows of a global store are 4 KiB
+          // apart (one per token), so stored from the threads directly each 16-byte store of a
+          // warp would touch 32 rows (32 L1 wavefronts per instruction, which also starves the
+          // other tile's P stores of the shared LSU).  The rows go through this tile's P buffer
+          // instead (free: its last P*V has completed) and each warp then writes whole rows: two
+          // adjacent 256-byte rows (one token's two heads) per instruction for the output, one
+          // 512-byte row per instruction for split-KV partials.  Staging layout: 256 bytes per row
+          // as 16 chunks of 16 bytes, chunk u of row r at chunk u ^ (r % 16), so the row-wise
+          // writes and the two-row reads are both free of bank conflicts.
           tc_fence_after();
           const float inv = l > 0.f ? 1.f / l : 0.f;
-          const int head = kvh * kGroup + (r & 1);
-          // Row inside the item's partial rows (split items have adjacent tiles: token order).
-          const int prow_r = t * 128 + r;
+          const uint32_t stg = smem_u32(smem + TcCfg::kPOff + t * TcCfg::kQBytes);
+          const int n_t = t == 0 ? n_a : n_b;
+          const int tok_t = t == 0 ? tok_a : tok_b;
+          const int wrow0 = (warp & 3) * 32;  // this warp's rows
+          const uint32_t rsw = static_cast<uint32_t>(r & 15);
+          // Columns [c0, c0 + 64) of this thread's row, scaled by 1 / l, into the staging row:
+          // bf16 (32 columns = 4 chunks) or fp32 (64 columns fill the whole 256-byte row).
+          auto stage_cols = [&](int c0, bool as_bf16) {
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            float ov[32];
-            if (nb > 0) {
-              tmem_ld32(o_addr + c * 32, ov);
-              tmem_wait_ld();
-            } else {
-#pragma unroll
-              for (int i = 0; i < 32; ++i) ov[i] = 0.f;
-            }
-            if (valid) {
-              if (part_row < 0) {
-                __nv_bfloat16* dst = a.out +
-                                     static_cast<long long>(flat_start + tok) * a.out_row_stride +
-                                     head * kHeadDim + c * 32;
-#pragma unroll
-                for (int u = 0; u < 4; ++u)
-                  reinterpret_cast<uint4*>(dst)[u] =
-                      make_uint4(pack_bf16(ov[8 * u] * inv, ov[8 * u + 1] * inv),
-                                 pack_bf16(ov[8 * u + 2] * inv, ov[8 * u + 3] * inv),
-                                 pack_bf16(ov[8 * u + 4] * inv, ov[8 * u + 5] * inv),
-                                 pack_bf16(ov[8 * u + 6] * inv, ov[8 * u + 7] * inv));
+            for (int c = 0; c < 2; ++c) {
+              float ov[32];
+              if (nb > 0) {
+                tmem_ld32(o_addr + c0 + c * 32, ov);
+                tmem_wait_ld();
               } else {
-                const long long prow = static_cast<long long>(part_row + prow_r) * a.num_kv + kvh;
-                float* dst = a.ws_o + prow * kHeadDim + c * 32;
 #pragma unroll
-                for (int u = 0; u < 8; ++u)
-                  reinterpret_cast<float4*>(dst)[u] = make_float4(
-                      ov[4 * u] * inv, ov[4 * u + 1] * inv, ov[4 * u + 2] * inv, ov[4 * u + 3] * inv);
-                if (c == 0) a.ws_lse[prow] = l > 0.f ? m + __log2f(l) : -INFINITY;
+                for (int i = 0; i < 32; ++i) ov[i] = 0.f;
               }
+              if (as_bf16) {
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                  const uint32_t chunk = static_cast<uint32_t>((c0 / 32 + c) * 4 + u);
+                  st_shared_v4(stg + r * 256 + ((chunk ^ rsw) << 4),
+                               pack_bf16(ov[8 * u] * inv, ov[8 * u + 1] * inv),
+                               pack_bf16(ov[8 * u + 2] * inv, ov[8 * u + 3] * inv),
+                               pack_bf16(ov[8 * u + 4] * inv, ov[8 * u + 5] * inv),
+                               pack_bf16(ov[8 * u + 6] * inv, ov[8 * u + 7] * inv));
+                }
+              } else {
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                  const uint32_t chunk = static_cast<uint32_t>(c * 8 + u);
+                  st_shared_v4(stg + r * 256 + ((chunk ^ rsw) << 4),
+                               __float_as_uint(ov[4 * u] * inv), __float_as_uint(ov[4 * u + 1] * inv),
+                               __float_as_uint(ov[4 * u + 2] * inv),
+                               __float_as_uint(ov[4 * u + 3] * inv));
+                }
+              }
+            }
+          };
+          const int u = lane & 15;
+          if (part_row < 0) {
+            stage_cols(0, true);
+            stage_cols(64, true);
+            __syncwarp();
+#pragma unroll 4
+            for (int i = 0; i < 16; ++i) {
+              const int R = wrow0 + 2 * i + (lane >> 4);
+              uint4 v;
+              asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                           : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                           : "r"(stg + R * 256 + ((static_cast<uint32_t>(u) ^ (R & 15)) << 4)));
+              if ((R >> 1) < n_t)
+                *reinterpret_cast<uint4*>(
+                    a.out + static_cast<long long>(flat_start + tok_t + (R >> 1)) * a.out_row_stride +
+                    (kvh * kGroup + (R & 1)) * kHeadDim + u * 8) = v;
+            }
+          } else {
+            // Row inside the item's partial rows (split items have adjacent tiles: token order).
+            if (valid) {
+              const long long prow = static_cast<long long>(part_row + t * 128 + r) * a.num_kv + kvh;
+              a.ws_lse[prow] = l > 0.f ? m + __log2f(l) : -INFINITY;
+            }
+#pragma unroll 1
+            for (int half = 0; half < 2; ++half) {
+              stage_cols(half * 64, false);
+              __syncwarp();
+#pragma unroll 4
+              for (int i = 0; i < 16; ++i) {
+                const int R = wrow0 + 2 * i + (lane >> 4);
+                uint4 v;
+                asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                             : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                             : "r"(stg + R * 256 + ((static_cast<uint32_t>(u) ^ (R & 15)) << 4)));
+                if ((R >> 1) < n_t) {
+                  const long long prow = static_cast<long long>(part_row + t * 128 + R) * a.num_kv + kvh;
+                  *reinterpret_cast<uint4*>(a.ws_o + prow * kHeadDim + half * 64 + u * 4) = v;
+                }
+              }
+              __syncwarp();  // the next half reuses the staging rows
             }
           }
         }

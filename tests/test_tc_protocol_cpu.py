@@ -8,6 +8,9 @@ timeout status bit after tens of milliseconds.  This test restates the protocol 
 agents over mbarrier phases (instant loads and MMAs: only the dependencies matter) and runs it to
 completion for every pair of per-tile block counts up to 40.
 
+The P*V issuer serves the two tiles of an entry in the order their P becomes ready (it polls
+both barriers), so the simulation lets it take whichever tile is ready.
+
 The simulator also runs a variant that was tried and not kept (the two warpgroups sharing the
 long tile's blocks and taking turns through their exponentials, with the second warpgroup taking
 two blocks ahead); that variant closes a wait cycle through the 3-slot ring, which shows that
@@ -106,14 +109,24 @@ def run_protocol(nb_a: int, nb_b: int, has_b: bool, shared: bool = False, lead: 
             empty[pos_k(w) % NS].arrive()
 
     def pv_issuer():
+        # Within an entry the shipped kernel issues the tiles in the order their P becomes ready
+        # (it polls both); the variant issues them in tile order.
         issued = [0, 0]
         for w, (_, slots) in enumerate(order):
             yield lambda p=pos_v(w): full[p % NS].done(p // NS)
-            for sl in (0, 1):
-                if (slots >> sl) & 1:
-                    yield lambda sl=sl, k=issued[sl]: p_full[sl].done(k)
+            pend = [sl for sl in (0, 1) if (slots >> sl) & 1]
+            while pend:
+                if turns:
+                    ready = [pend[0]]
+                    yield lambda sl=pend[0], k=issued[pend[0]]: p_full[sl].done(k)
+                else:
+                    yield lambda pend=tuple(pend), k=tuple(issued): any(
+                        p_full[sl].done(k[sl]) for sl in pend)
+                    ready = [sl for sl in pend if p_full[sl].done(issued[sl])]
+                for sl in ready:
                     pv_done[sl].arrive()
                     issued[sl] += 1
+                    pend.remove(sl)
             empty[pos_v(w) % NS].arrive()
 
     def softmax(sl: int):
