@@ -551,11 +551,17 @@ def run_prefill_only(rank: int, device: torch.device) -> None:
                       "timing": "CUDA-graph replay of 10 calls, best of 5, per call"}), flush=True)
 
 
-def run_e2e(ws: DeviceStep, args: argparse.Namespace, world: int) -> tuple[float, int, int]:
+def run_e2e(ws: DeviceStep, args: argparse.Namespace, world: int
+            ) -> tuple[float, float, int, int]:
     """The same step through the public Python API with host buffers: each step prepares its
     positions and slot mapping from the block tables (ms_prepare_step), plans (ms_plan_build)
     and uploads the plan, copies every layer's qkv up from pinned host memory and every layer's
-    output back.  Returns (ms for args.steps steps, H2D bytes per step, D2H bytes per step)."""
+    output back.  Two forms: eager (every layer's calls made from Python each step) and replayed
+    (the device part of a step -- cos/sin rows, every layer's copies and kernels -- captured once
+    as a CUDA graph; each step prepares and plans on the host, writes positions, slots and plan
+    into the captured buffers with AttentionMetadata.update, and replays).  Returns (ms of the
+    replayed form and of the eager form for args.steps steps, H2D bytes per step, D2H bytes per
+    step)."""
     from miniserve_b200.attention import attend, build_attention_metadata, prepare_arrays
     from miniserve_b200.qwen3_attention import qk_norm_rope_scatter
 
@@ -634,11 +640,81 @@ def run_e2e(ws: DeviceStep, args: argparse.Namespace, world: int) -> tuple[float
     for _ in range(max(1, args.warmup)):
         e2e_step()
     torch.cuda.synchronize(device)
-    e2e_ms = ws.timed(e2e_step, args.steps, world)
+    eager_ms = ws.timed(e2e_step, args.steps, world)
+
+    # Replayed form.  Positions, slots and plan live in buffers the graph captured; the host
+    # writes each step's values into them on the stream (after the previous replay's kernels).
+    pos_dev = torch.empty(t, dtype=torch.int64, device=device)
+    slot_dev = torch.empty(t, dtype=torch.int64, device=device)
+    prepare_arrays(new_np, cached_np, offsets_np, tables_np, pos_bufs[0].numpy(),
+                   slot_bufs[0].numpy())
+    pos_dev.copy_(pos_bufs[0])
+    slot_dev.copy_(slot_bufs[0])
+    meta_g = build_attention_metadata(batch.chunks, slot_dev, 16, pages_per_split=ws.pages_per_split)
+
+    def device_part() -> None:
+        cur = torch.cuda.current_stream(device)
+        c, s = ws.cos_t[pos_dev], ws.sin_t[pos_dev]
+        if not overlap_copies:
+            qkv_dev.copy_(qkv_host, non_blocking=True)
+            for layer in range(layers):
+                k_cache, v_cache = ws.views[layer]
+                q = qk_norm_rope_scatter(qkv_dev[layer], ws.qw[layer], ws.kw[layer], 1e-6, c, s,
+                                         slot_dev, k_cache, v_cache, H, q_out=ws.q_buf)
+                attend(q, k_cache, v_cache, meta_g, D**-0.5, out=ws.out_all[layer])
+            out_host.copy_(ws.out_all, non_blocking=True)
+            return
+        step_started.record(cur)
+        with torch.cuda.stream(copy_stream):
+            copy_stream.wait_event(step_started)
+            for layer in range(layers):
+                qkv_dev[layer].copy_(qkv_host[layer], non_blocking=True)
+                qkv_arrived[layer].record(copy_stream)
+        for layer in range(layers):
+            k_cache, v_cache = ws.views[layer]
+            cur.wait_event(qkv_arrived[layer])
+            q = qk_norm_rope_scatter(qkv_dev[layer], ws.qw[layer], ws.kw[layer], 1e-6, c, s,
+                                     slot_dev, k_cache, v_cache, H, q_out=ws.q_buf)
+            attend(q, k_cache, v_cache, meta_g, D**-0.5, out=ws.out_all[layer])
+            out_written[layer].record(cur)
+            with torch.cuda.stream(copy_stream):
+                copy_stream.wait_event(out_written[layer])
+                out_host[layer].copy_(ws.out_all[layer], non_blocking=True)
+        cur.wait_stream(copy_stream)
+
+    device_part()
+    torch.cuda.synchronize(device)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        device_part()
+    torch.cuda.synchronize(device)
+
+    def replay_step() -> None:
+        k = step_no[0] & 1
+        step_no[0] += 1
+        if copies_done[k] is not None:
+            copies_done[k].synchronize()
+        prepare_arrays(new_np, cached_np, offsets_np, tables_np, pos_bufs[k].numpy(),
+                       slot_bufs[k].numpy())
+        pos_dev.copy_(pos_bufs[k], non_blocking=True)
+        slot_dev.copy_(slot_bufs[k], non_blocking=True)
+        done = torch.cuda.Event()
+        done.record(stream)
+        copies_done[k] = done
+        if not meta_g.update(batch.chunks):
+            raise RuntimeError("the step's plan no longer matches the captured launch shape")
+        graph.replay()
+
+    for _ in range(max(1, args.warmup)):
+        replay_step()
+    torch.cuda.synchronize(device)
+    graph_ms = ws.timed(replay_step, args.steps, world)
+    torch.cuda.synchronize(device)
+    del graph
     h2d = qkv_host.numel() * 2 + pos_bufs[0].numel() * 8 + slot_bufs[0].numel() * 8 \
         + int(ws.meta.info.total_ints) * 4
     d2h = out_host.numel() * 2
-    return e2e_ms, h2d, d2h
+    return graph_ms, eager_ms, h2d, d2h
 
 
 def run_headline(args: argparse.Namespace, rank: int, world: int, device: torch.device) -> dict:
@@ -682,12 +758,12 @@ def run_headline(args: argparse.Namespace, rank: int, world: int, device: torch.
                                        ws.slot_mapping, ws.layers, device, ws.stream)
         ws.check_status("after the qkv projection timing")
 
-    e2e_ms, h2d, d2h = run_e2e(ws, args, world)
+    e2e_ms, e2e_eager_ms, h2d, d2h = run_e2e(ws, args, world)
     attn_bytes, a_bytes, attn_flops = attention_bytes(batch)
     info = ws.meta.info
     res = {
         "total_ms": total_ms, "eager_ms": eager_ms, "graph": ws.graph is not None,
-        "e2e_ms": e2e_ms, "attn_ms": attn_ms, "attn_bytes": attn_bytes,
+        "e2e_ms": e2e_ms, "e2e_eager_ms": e2e_eager_ms, "attn_ms": attn_ms, "attn_bytes": attn_bytes,
         "attn_flops": attn_flops, "logical_kv_tokens": batch.kv_tokens_read(),
         "kernel_a_bytes": a_bytes, "tokens": batch.num_tokens,
         "kv_tokens": (batch.kv_tokens_read() if ws.alias else batch.unique_kv_tokens()),
@@ -949,7 +1025,7 @@ def main() -> None:
     r = run_headline(args, rank, world, device)
     hbm = float(peaks()[0]["hbm_gbs"])
     my_achieved = r["attn_bytes"] / (r["attn_ms"] * 1e-3) / 1e9
-    ms = torch.tensor([r["total_ms"], r["e2e_ms"], r["attn_ms"], r["eager_ms"]],
+    ms = torch.tensor([r["total_ms"], r["e2e_ms"], r["attn_ms"], r["eager_ms"], r["e2e_eager_ms"]],
                       dtype=torch.float64, device=device)
     toks = torch.tensor([r["tokens"]], dtype=torch.float64, device=device)
     mine = torch.tensor([my_achieved, r["attn_ms"], r["attn_bytes"]], dtype=torch.float64,
@@ -962,7 +1038,7 @@ def main() -> None:
     else:
         every = [mine]
     per_rank = [x.cpu().tolist() for x in every]
-    total_ms, e2e_ms, attn_ms_max, eager_ms = (float(x) for x in ms.cpu())
+    total_ms, e2e_ms, attn_ms_max, eager_ms, e2e_eager_ms = (float(x) for x in ms.cpu())
     ms_per_step = total_ms / args.steps
     e2e_per_step = e2e_ms / args.steps
     tokens_all = int(toks.item())
@@ -1032,11 +1108,16 @@ def main() -> None:
             "cpu_baseline": cpu,
             "e2e": {"value": tokens_all / (e2e_per_step * 1e-3), "unit": "tok/s",
                     "h2d_bytes_per_step": r["h2d"], "d2h_bytes_per_step": r["d2h"],
+                    "eager_value": tokens_all / (e2e_eager_ms / args.steps * 1e-3),
                     "host_work_per_step": "ms_prepare_step (positions, slots) + ms_plan_build "
-                                          "+ one plan upload; qkv of all layers in, outputs of "
-                                          "all layers out (per layer on a copy stream, "
+                                          "+ the plan written into the captured step's buffers "
+                                          "(AttentionMetadata.update) + one CUDA-graph replay of "
+                                          "the step's device part: qkv of all layers in, outputs "
+                                          "of all layers out (per layer on a copy stream, "
                                           "overlapped with the other layers' kernels, when a "
-                                          "layer's input is >= 1 MiB)"},
+                                          "layer's input is >= 1 MiB), cos/sin rows, every "
+                                          "layer's kernels; eager_value: the same with every "
+                                          "layer's calls made from Python each step"},
             "gpu_launches": r["launches_per_step"] * args.steps,
             "clocks": r["clocks"],
             "plan": r["plan"],

@@ -56,6 +56,32 @@ class AttentionMetadata:
     info: _capi.MsPlanInfo  # host-side description of the plan
     num_tokens: int
     _workspace: dict[tuple[int, int], Tensor] = field(default_factory=dict, repr=False)
+    _num_sms: int = field(default=148, repr=False)
+    _pages_per_split: int = field(default=0, repr=False)
+
+    def update(self, chunks: list[SeqChunk], slot_mapping: Tensor | None = None) -> bool:
+        """Plan a new step into this metadata's device buffers, for CUDA-graph replay.
+
+        A graph captured over calls that use this metadata keeps the addresses of its plan and
+        slot mapping and the launch shapes derived from ``info`` (grid sizes, section offsets,
+        workspace size).  When the new step's plan has the same shape (same item counts, offsets
+        and split workspace: for example, the same batch again, or contexts that grew inside their
+        last pages), its plan and, if given, its slot mapping are copied into the existing buffers
+        on the current stream (after the work already queued there, so no kernel of the previous
+        step sees them) and True is returned.  Otherwise nothing changes and False is returned:
+        build new metadata and capture again.  No reference counterpart (MiniServe captures no
+        graphs).
+        """
+        if slot_mapping is not None and tuple(slot_mapping.shape) != tuple(self.slot_mapping.shape):
+            return False
+        packed, info = plan_batch(chunks, self.num_tokens, BLOCK_SIZE, self._num_sms,
+                                  self._pages_per_split)
+        if not same_launch_shape(info, self.info):
+            return False
+        self.plan.copy_(torch.from_numpy(packed).pin_memory(), non_blocking=True)
+        if slot_mapping is not None and slot_mapping.data_ptr() != self.slot_mapping.data_ptr():
+            self.slot_mapping.copy_(slot_mapping, non_blocking=True)
+        return True
 
     def workspace(self, num_kv_heads: int, device: torch.device) -> Tensor | None:
         """Split-KV scratch for this step (allocated once, reused by every layer)."""
@@ -188,7 +214,17 @@ def build_attention_metadata(
     packed, info = plan_batch(chunks, num_tokens, block_size, num_sms, pages_per_split)
     plan = _upload_plan(packed, device)
     slots = slot_mapping if slot_mapping.dtype == torch.int64 else slot_mapping.to(torch.int64)
-    return AttentionMetadata(slots.contiguous(), plan, info, num_tokens)
+    return AttentionMetadata(slots.contiguous(), plan, info, num_tokens,
+                             _num_sms=num_sms, _pages_per_split=pages_per_split)
+
+
+def same_launch_shape(a: _capi.MsPlanInfo, b: _capi.MsPlanInfo) -> bool:
+    """Whether two plans launch the same kernels with the same arguments apart from the plan's
+    contents: every field of the plan description is equal except the total page count (a
+    statistic no launch reads)."""
+    return all(getattr(a, name) == getattr(b, name)
+               for name, _ in _capi.MsPlanInfo._fields_
+               if name not in ("total_pages", "reserved"))
 
 
 def _upload_plan(packed: np.ndarray, device: torch.device) -> Tensor:

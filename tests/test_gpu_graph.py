@@ -76,3 +76,73 @@ def test_graph_replay_matches_eager(workload: str, cuda_device: torch.device) ->
         step()
         torch.cuda.synchronize(dev)
         assert torch.equal(replayed, out), trial
+
+
+def test_graph_replay_after_metadata_update(cuda_device: torch.device) -> None:
+    """A step captured with one batch, replayed after ``AttentionMetadata.update`` has written a
+    different batch of the same launch shape into its buffers (the same contexts, other pages:
+    every block id remapped), equals an eager run of the new batch with freshly built metadata,
+    bit for bit.  A batch of another shape is refused and leaves the metadata as it was."""
+    from miniserve_b200.attention import SeqChunk
+
+    dev = cuda_device
+    layers, batch = 4, config2(seed=7, num_seqs=32)
+    t = batch.num_tokens
+    g = torch.Generator(device=dev).manual_seed(7)
+    pool, views = allocate_kv_cache(layers, batch.num_blocks, 8, dev, zero=False)
+    pool.normal_(generator=g)
+    pool_copy = pool.clone()
+    qkv = torch.randn(layers, t, 4096, generator=g, device=dev, dtype=torch.bfloat16)
+    qw = (1 + 0.1 * torch.randn(layers, 128, generator=g, device=dev)).bfloat16()
+    kw = (1 + 0.1 * torch.randn(layers, 128, generator=g, device=dev)).bfloat16()
+    cos_t, sin_t = rope_tables(128, batch.max_position + 8, 1e6, dev)
+    pos = torch.from_numpy(batch.positions).to(dev)
+    cos, sin = cos_t[pos], sin_t[pos]
+    slots = torch.from_numpy(batch.slots).to(dev)
+    meta = build_attention_metadata(batch.chunks, slots, 16, pages_per_split=16)
+    assert meta.info.n_combine > 0
+    q_buf = torch.empty(t, 16, 128, dtype=torch.bfloat16, device=dev)
+    out = torch.empty(layers, t, 16, 128, dtype=torch.bfloat16, device=dev)
+
+    def step(m) -> None:
+        for i in range(layers):
+            kc, vc = views[i]
+            qk_norm_rope_scatter(qkv[i], qw[i], kw[i], 1e-6, cos, sin, m.slot_mapping, kc, vc, 16,
+                                 q_out=q_buf)
+            attend(q_buf, kc, vc, m, 128**-0.5, out=out[i])
+
+    step(meta)
+    torch.cuda.synchronize(dev)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step(meta)
+
+    # The same contexts on other pages.
+    perm = torch.randperm(batch.num_blocks, generator=torch.Generator().manual_seed(8))
+    chunks_b = [SeqChunk(c.flat_start, c.num_new, c.num_cached, [int(perm[b]) for b in c.block_table])
+                for c in batch.chunks]
+    slots_cpu = torch.from_numpy(batch.slots)
+    slots_b = (perm[slots_cpu // 16] * 16 + slots_cpu % 16).to(dev)
+    assert meta.update(chunks_b, slots_b)
+    qkv.copy_(torch.randn(layers, t, 4096, generator=g, device=dev, dtype=torch.bfloat16))
+    pool.copy_(pool_copy)
+    graph.replay()
+    torch.cuda.synchronize(dev)
+    replayed = out.clone()
+    pool.copy_(pool_copy)
+    step(build_attention_metadata(chunks_b, slots_b, 16, pages_per_split=16))
+    torch.cuda.synchronize(dev)
+    assert torch.equal(replayed, out)
+
+    # Another shape (one context grows into a new page) is refused; nothing is written.
+    plan_before = meta.plan.clone()
+    grown = list(chunks_b)
+    c0 = grown[0]
+    pages = (c0.num_cached + 1 + 15) // 16
+    extra = 16 * pages - c0.num_cached  # cached tokens that move the last token to a new page
+    used = {b for c in chunks_b for b in c.block_table}
+    free = next(b for b in range(batch.num_blocks) if b not in used)
+    grown[0] = SeqChunk(c0.flat_start, 1, c0.num_cached + extra, c0.block_table[:pages] + [free])
+    assert not meta.update(grown)
+    torch.cuda.synchronize(dev)
+    assert torch.equal(meta.plan, plan_before)
