@@ -157,23 +157,35 @@ __device__ __forceinline__ void attend_page(uint32_t stage, const uint32_t (&qf)
   }
 }
 
-__device__ unsigned g_status_word;  // device status bits (kErr*), read by ms_device_status
+__device__ unsigned g_status_word;
+
+// Named barrier 1 or 2 (bar_id) for `threads` threads, with the id a constant in the instruction
+// (a barrier id held in a register makes the compiler reserve all 16 named barriers).
+__device__ __forceinline__ void named_bar_1_or_2(int bar_id, int threads) {
+  if (bar_id == 1)
+    asm volatile("bar.sync 1, %0;" ::"r"(threads) : "memory");
+  else
+    asm volatile("bar.sync 2, %0;" ::"r"(threads) : "memory");
+}  // device status bits (kErr*), read by ms_device_status
 
 // Decode mode: merge the consumer warps' (m, l, O) over their page subsets through `merge`
 // (kConsumerWarps x 16 x (128 + 4) fp32 accumulators, then kConsumerWarps x 16 maxima and as many
 // sums) and write the rows: bf16 output (merged with a cascade row's shared-prefix partial when
-// merge_row >= 0) or fp32 partial rows and log2-sum-exp for split items.  Called by every
-// consumer thread (threadIdx.x < 32 * kConsumerWarps); uses named barrier 1.
+// merge_row >= 0) or fp32 partial rows and log2-sum-exp for split items.  Called by the
+// kConsumerWarps warps that attended the item (warp = 0 .. kConsumerWarps - 1 among them, tid =
+// 0 .. 32 kConsumerWarps - 1), which synchronise on named barrier bar_id.
 template <int kConsumerWarps, bool kWaitBeforeMerge = false>
 __device__ __forceinline__ void decode_merge_store(float* merge, const float (&o)[16][4],
                                                    const float (&m)[2], const float (&l)[2],
                                                    int warp, int lane, int n_q, int kvh,
                                                    int part_row, int merge_row, int flat_start,
-                                                   int tok0, const AttnArgs& a) {
+                                                   int tok0, const AttnArgs& a, int bar_id = 1,
+                                                   int tid = -1) {
+  if (tid < 0) tid = threadIdx.x;
   float* mo = merge;
   float* mm = mo + kConsumerWarps * 16 * (kHeadDim + 4);
   float* ml = mm + kConsumerWarps * 16;
-  asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
+  named_bar_1_or_2(bar_id, kConsumerWarps * 32);
   {
     float* wo = mo + warp * 16 * (kHeadDim + 4);
     const int ra = lane >> 2, rb = ra + 8, c = 2 * (lane & 3);
@@ -189,8 +201,7 @@ __device__ __forceinline__ void decode_merge_store(float* merge, const float (&o
       ml[warp * 16 + rb] = l[1];
     }
   }
-  asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
-  const int tid = threadIdx.x;
+  named_bar_1_or_2(bar_id, kConsumerWarps * 32);
   for (int e = tid; e < 16 * 8; e += kConsumerWarps * 32) {
     const int r = e >> 3;
     const int dc = (e & 7) * 16;
@@ -552,19 +563,29 @@ __global__ void __launch_bounds__(AttnCfg<kMode, kConsumerWarps, kStages>::kThre
 
 // Decode mode, persistent over work units (unit u = (item u / num_kv, KV head u % num_kv); CTA c
 // takes units c, c + G, c + 2G, ...) for plans of many short items, where a one-unit CTA spends
-// most of its life starting up and finishing: here the producer streams the next unit's pages
-// while the consumers finish the current one, and each unit's query rows are loaded into
-// registers during the previous unit.  Per unit the consumer work is kernel B's decode mode (the
-// same attend_page and decode_merge_store), so the results are the same bit for bit; the merge
-// scratch has its own shared memory because the ring keeps streaming.
+// most of its life starting up and finishing: here the producers stream the next units' pages
+// while the consumers finish the current ones, and each unit's query rows are copied into shared
+// memory during the group's previous unit.  Per unit the consumer work is kernel B's decode mode
+// (the same attend_page and decode_merge_store) with the unit's pages split over the group's
+// warps instead of all consumer warps, so the results equal kernel B's up to the order in which
+// the per-warp partial sums are merged; the merge scratch has its own shared memory because the
+// ring keeps streaming.
 template <int kConsumerWarps, int kStages>
 struct UnitsCfg {
   using Base = AttnCfg<0, kConsumerWarps, kStages>;
-  static constexpr int kThreads = Base::kThreads;
+  // The consumer warps form kGroups groups that take alternate units.  Each group has its own
+  // producer warp, kGroupStages slots of the ring, query tile and merge scratch.
+  static constexpr int kGroups = 2;
+  static constexpr int kGroupWarps = kConsumerWarps / kGroups;
+  static constexpr int kGroupStages = kStages / kGroups;
+  static_assert(kConsumerWarps % kGroups == 0 && kStages % kGroups == 0, "even split");
+  static constexpr int kThreads = (kConsumerWarps + kGroups) * 32;
   static constexpr int kStageBytes = Base::kStageBytes;
-  static constexpr int kQBytes = Base::kQBytes;
-  static constexpr int kMergeOff = kStageBytes + kQBytes;
-  static constexpr int kMergeBytes = kConsumerWarps * 16 * (kHeadDim + 4) * 4 + 2 * kConsumerWarps * 16 * 4;
+  static constexpr int kQBytes = Base::kQBytes;  // per group
+  static constexpr int kMergeOff = kStageBytes + kGroups * kQBytes;
+  static constexpr int kGroupMergeBytes =
+      kGroupWarps * 16 * (kHeadDim + 4) * 4 + 2 * kGroupWarps * 16 * 4;  // per group
+  static constexpr int kMergeBytes = kGroups * kGroupMergeBytes;
   static constexpr int kBarOffset = kMergeOff + kMergeBytes;
   static constexpr int kSmemBytes = 1024 + kBarOffset + 2 * kStages * 8 + 16;
 };
@@ -607,13 +628,22 @@ __global__ void __launch_bounds__(UnitsCfg<kConsumerWarps, kStages>::kThreads, 2
   }
   __syncthreads();
 
-  if (warp == kConsumerWarps) {
-    // ---------------- producer warp: every unit's pages, in order, through one ring ----------
+  // Group gi takes the CTA's units u = blockIdx.x + (kGroups i + gi) gridDim.x, i = 0, 1, ...
+  constexpr int kGS = Cfg::kGroupStages;
+  const int ustep = Cfg::kGroups * static_cast<int>(gridDim.x);
+  if (warp >= kConsumerWarps) {
+    // ---------------- producer warps: one per group, the group's pages in order through the
+    // group's own kGS slots of the ring -----------------------------------------------------
+    const int pg = warp - kConsumerWarps;
     const uint64_t policy = l2_policy_evict_first();
     if (lane == 0) tma_prefetch_desc(&kv_map);
-    int g = 0;  // pages issued so far (over all of this CTA's units)
+    uint64_t* gfull = full + pg * kGS;
+    uint64_t* gempty = empty + pg * kGS;
+    uint8_t* gring = ring + pg * kGS * kPageKVBytes;
+    int g = 0;  // pages issued so far (over all of this group's units)
     bool stop = false;
-    for (int u = blockIdx.x; u < n_units && !stop; u += gridDim.x) {
+    for (int u = static_cast<int>(blockIdx.x) + pg * static_cast<int>(gridDim.x);
+         u < n_units && !stop; u += ustep) {
       const int item_idx = u / a.num_kv;
       const int kvh = u - item_idx * a.num_kv;
       const int* it = a.items + static_cast<long long>(item_idx) * kRec;
@@ -628,9 +658,9 @@ __global__ void __launch_bounds__(UnitsCfg<kConsumerWarps, kStages>::kThreads, 2
           const int blk = __shfl_sync(0xffffffffu, mine, jj);
           int ok = 1;
           if (lane == 0) {
-            const int s = g % kStages;
+            const int s = g % kGS;
             if (*abort_flag) ok = 0;
-            if (ok && g >= kStages && !mbar_wait(&empty[s], ((g / kStages) - 1) & 1)) {
+            if (ok && g >= kGS && !mbar_wait(&gempty[s], ((g / kGS) - 1) & 1)) {
               atomicOr(&g_status_word, kErrTimeout);
               *abort_flag = 1;
               ok = 0;
@@ -639,8 +669,8 @@ __global__ void __launch_bounds__(UnitsCfg<kConsumerWarps, kStages>::kThreads, 2
               // Out-of-range block ids are flagged; the TMA unit fills such boxes with zeros.
               if (static_cast<unsigned>(blk) >= static_cast<unsigned>(a.num_blocks))
                 atomicOr(&g_status_word, kErrBlock);
-              mbar_arrive_expect_tx(&full[s], kPageKVBytes);
-              tma_load_5d(ring + s * kPageKVBytes, &kv_map, &full[s], 0, 0, 0, kvh, blk, policy);
+              mbar_arrive_expect_tx(&gfull[s], kPageKVBytes);
+              tma_load_5d(gring + s * kPageKVBytes, &kv_map, &gfull[s], 0, 0, 0, kvh, blk, policy);
             }
           }
           ok = __shfl_sync(0xffffffffu, ok, 0);
@@ -654,8 +684,8 @@ __global__ void __launch_bounds__(UnitsCfg<kConsumerWarps, kStages>::kThreads, 2
     }
     // Drain: never leave the CTA with a TMA write in flight.
     if (lane == 0) {
-      for (int j = g > kStages ? g - kStages : 0; j < g; ++j) {
-        if (!mbar_wait(&full[j % kStages], (j / kStages) & 1)) {
+      for (int j = g > kGS ? g - kGS : 0; j < g; ++j) {
+        if (!mbar_wait(&gfull[j % kGS], (j / kGS) & 1)) {
           atomicOr(&g_status_word, kErrTimeout);
           break;
         }
@@ -666,11 +696,25 @@ __global__ void __launch_bounds__(UnitsCfg<kConsumerWarps, kStages>::kThreads, 2
   }
 
   // ---------------- consumer warps ----------------
+  // Two groups of consumer warps take the CTA's units alternately, so one group's merge and
+  // output run while the other group attends its unit's pages: a unit holds ~10 pages, and with
+  // all warps on one unit no page was taken during a merge.  Within a group the warps split the
+  // unit's pages; each group has its own producer, ring slots, query tile, merge scratch and
+  // named barrier (1 + group).  The groups share no slot: a slot's full barrier is waited on by
+  // parity, which is exact only while the slot's previous fill has completed, and within a group
+  // that previous fill is always a page the same warp (or the group's previous unit) consumed.
+  constexpr int kGW = Cfg::kGroupWarps;
+  const int grp = warp / kGW;
+  const int gw = warp - grp * kGW;                 // warp within the group
+  const int gtid = threadIdx.x - grp * kGW * 32;   // thread within the group
+  const int bar_id = 1 + grp;
   // A unit's 16 query rows (token r / 2, head kvh * 2 + r % 2), 16 chunks of 16 bytes each,
-  // kPer chunks per consumer thread, loaded into registers one unit ahead.
-  constexpr int kPer = 16 * 16 / (kConsumerWarps * 32);
-  static_assert(16 * 16 % (kConsumerWarps * 32) == 0, "query chunks per thread");
-  auto load_q = [&](int u, uint4 (&v)[kPer]) {
+  // kPer chunks per thread of the group, copied into the group's query tile one unit ahead
+  // (cp.async: no registers held across the page loop).
+  constexpr int kPer = 16 * 16 / (kGW * 32);
+  static_assert(16 * 16 % (kGW * 32) == 0, "query chunks per thread");
+  const uint32_t qbase_s = smem_u32(qtile + grp * Cfg::kQBytes);
+  auto prefetch_q = [&](int u) {
     const int item_idx = u / a.num_kv;
     const int kvh = u - item_idx * a.num_kv;
     const int* it = a.items + static_cast<long long>(item_idx) * kRec;
@@ -678,23 +722,29 @@ __global__ void __launch_bounds__(UnitsCfg<kConsumerWarps, kStages>::kThreads, 2
     const int flat_start = a.seqs[static_cast<long long>(it[0]) * kRec];
 #pragma unroll
     for (int k = 0; k < kPer; ++k) {
-      const int c = threadIdx.x + k * kConsumerWarps * 32;
+      const int c = gtid + k * kGW * 32;
       const int r = c >> 4;
       const int d = (c & 15) * 8;
       const int tok = r >> 1;
-      v[k] = make_uint4(0u, 0u, 0u, 0u);
-      if (tok < n_q)
-        v[k] = __ldg(reinterpret_cast<const uint4*>(
-            a.q + static_cast<long long>(flat_start + tok0 + tok) * a.q_row_stride +
-            (kvh * kGroup + (r & 1)) * kHeadDim + d));
+      const uint32_t dst = qbase_s + swz_off(r, d, 16);
+      if (tok < n_q) {
+        const __nv_bfloat16* src = a.q + static_cast<long long>(flat_start + tok0 + tok) * a.q_row_stride +
+                                   (kvh * kGroup + (r & 1)) * kHeadDim + d;
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+      } else {
+        asm volatile("st.shared.v4.b32 [%0], {%1, %1, %1, %1};" ::"r"(dst), "r"(0u) : "memory");
+      }
     }
+    asm volatile("cp.async.commit_group;" ::: "memory");
   };
-  uint4 qn[kPer];
-  if (blockIdx.x < static_cast<unsigned>(n_units)) load_q(blockIdx.x, qn);
-  const uint32_t ring_u32 = smem_u32(ring);
-  const uint32_t qbase_s = smem_u32(qtile);
-  int g0 = 0;  // this unit's first page in the ring sequence
-  for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
+  const int u_first = static_cast<int>(blockIdx.x) + grp * static_cast<int>(gridDim.x);
+  if (u_first < n_units) prefetch_q(u_first);
+  const uint32_t ring_u32 = smem_u32(ring + grp * kGS * kPageKVBytes);
+  uint64_t* gfull = full + grp * kGS;
+  uint64_t* gempty = empty + grp * kGS;
+  float* merge_g = merge + grp * (Cfg::kGroupMergeBytes / 4);
+  int g0 = 0;  // this unit's first page in the group's ring sequence
+  for (int u = u_first; u < n_units; u += ustep) {
     const int item_idx = u / a.num_kv;
     const int kvh = u - item_idx * a.num_kv;
     const int* it = a.items + static_cast<long long>(item_idx) * kRec;
@@ -705,19 +755,10 @@ __global__ void __launch_bounds__(UnitsCfg<kConsumerWarps, kStages>::kThreads, 2
     const int flat_start = sr[0], num_cached = sr[2];
     const int npages = page_end - page_begin;
 
-    // The previous unit's merge has finished with the query tile and the merge scratch.
-    asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
-#pragma unroll
-    for (int k = 0; k < kPer; ++k) {
-      const int c = threadIdx.x + k * kConsumerWarps * 32;
-      const int r = c >> 4;
-      const int d = (c & 15) * 8;
-      asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(
-                       qbase_s + (r >> 4) * (16 * kHeadDim * 2) + swz_off(r & 15, d, 16)),
-                   "r"(qn[k].x), "r"(qn[k].y), "r"(qn[k].z), "r"(qn[k].w)
-                   : "memory");
-    }
-    asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
+    // This unit's query tile has landed (every thread's copies), and the group's previous unit
+    // has finished with the merge scratch.
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    named_bar_1_or_2(bar_id, kGW * 32);
     uint32_t qf[8][4];
     {
       const int mi = lane >> 3;
@@ -727,7 +768,9 @@ __global__ void __launch_bounds__(UnitsCfg<kConsumerWarps, kStages>::kThreads, 2
         ldsm_x4(qbase_s + swz_off(row, ks * 16 + (mi >> 1) * 8, 16), qf[ks][0], qf[ks][1],
                 qf[ks][2], qf[ks][3]);
     }
-    if (u + static_cast<int>(gridDim.x) < n_units) load_q(u + gridDim.x, qn);
+    // Every warp of the group holds its query fragments: the tile takes the next unit's rows.
+    named_bar_1_or_2(bar_id, kGW * 32);
+    if (u + ustep < n_units) prefetch_q(u + ustep);
 
     float o[16][4];
 #pragma unroll
@@ -741,12 +784,12 @@ __global__ void __launch_bounds__(UnitsCfg<kConsumerWarps, kStages>::kThreads, 2
     const int qpos1 = qpos_base + (r1 >> 1);
     const int min_qpos = qpos_base;
     const int max_qpos = qpos_base + 7;
-    for (int j = warp; j < npages; j += kConsumerWarps) {
+    for (int j = gw; j < npages; j += kGW) {
       const int gj = g0 + j;
-      const int s = gj % kStages;
+      const int s = gj % kGS;
       // Leave the loop only as a whole warp: the tensor-core ops below are warp-collective.
       const bool ok =
-          __all_sync(0xffffffffu, mbar_wait_fast(&full[s], (gj / kStages) & 1, abort_flag));
+          __all_sync(0xffffffffu, mbar_wait_fast(&gfull[s], (gj / kGS) & 1, abort_flag));
       if (!ok) {
         if (lane == 0) {
           atomicOr(&g_status_word, kErrTimeout);
@@ -760,15 +803,15 @@ __global__ void __launch_bounds__(UnitsCfg<kConsumerWarps, kStages>::kThreads, 2
                     key0 + kBlockTokens - 1 > min_qpos, a.scale_log2, lane);
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[s]);
+      if (lane == 0) mbar_arrive(&gempty[s]);
     }
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
       l[i] += __shfl_xor_sync(0xffffffffu, l[i], 1);
       l[i] += __shfl_xor_sync(0xffffffffu, l[i], 2);
     }
-    decode_merge_store<kConsumerWarps, kAfterPrefix>(merge, o, m, l, warp, lane, n_q, kvh,
-                                                     part_row, merge_row, flat_start, tok0, a);
+    decode_merge_store<kGW, kAfterPrefix>(merge_g, o, m, l, gw, lane, n_q, kvh, part_row,
+                                          merge_row, flat_start, tok0, a, bar_id, gtid);
     g0 += npages;
   }
   if constexpr (kAfterPrefix) pdl_wait();
