@@ -469,22 +469,22 @@ __global__ void __launch_bounds__(TcCfg::kThreads, 1)
           uint32_t pk[4][16];
           float alpha = 1.f;
           bool rescale = false;
+          float s0[32], s1[32], s2[32], s3[32];
+          tmem_ld32(s_addr, s0);
+          tmem_ld32(s_addr + 32, s1);
+          tmem_ld32(s_addr + 64, s2);
+          tmem_ld32(s_addr + 96, s3);
+          tmem_wait_ld();
+          tc_fence_before();
+          mbar_arrive(&s_free[t]);  // the MMA may now overwrite S_t with S_t(j + 1)
+          if (need_mask) {
+            const int lim = min(qpos + 1, key_end) - k0;
+            mask_scores32(s0, lim);
+            mask_scores32(s1, lim - 32);
+            mask_scores32(s2, lim - 64);
+            mask_scores32(s3, lim - 96);
+          }
           {
-            float s0[32], s1[32], s2[32], s3[32];
-            tmem_ld32(s_addr, s0);
-            tmem_ld32(s_addr + 32, s1);
-            tmem_ld32(s_addr + 64, s2);
-            tmem_ld32(s_addr + 96, s3);
-            tmem_wait_ld();
-            tc_fence_before();
-            mbar_arrive(&s_free[t]);  // the MMA may now overwrite S_t with S_t(j + 1)
-            if (need_mask) {
-              const int lim = min(qpos + 1, key_end) - k0;
-              mask_scores32(s0, lim);
-              mask_scores32(s1, lim - 32);
-              mask_scores32(s2, lim - 64);
-              mask_scores32(s3, lim - 96);
-            }
             const float mx = max128(s0, s1, s2, s3) * a.scale_log2;
             // The running max m only moves (and O is rescaled) when the block's max exceeds it by
             // more than 2^8.
@@ -493,17 +493,13 @@ __global__ void __launch_bounds__(TcCfg::kThreads, 1)
               rescale = j > 0;
               m = mx;
             }
-            const float neg_mu = m == ninf ? 0.f : -m;
-            const float2 nm2 = make_float2(neg_mu, neg_mu);
-            exp_pack32(s0, sc2, nm2, suma, pk[0]);
-            exp_pack32(s1, sc2, nm2, suma, pk[1]);
-            exp_pack32(s2, sc2, nm2, suma, pk[2]);
-            exp_pack32(s3, sc2, nm2, suma, pk[3]);
           }
-          const float2 s01 = __fadd2_rn(suma[0], suma[1]);
-          const float2 s23 = __fadd2_rn(suma[2], suma[3]);
-          const float2 st = __fadd2_rn(s01, s23);
-          l = l * alpha + (st.x + st.y);
+          const float neg_mu = m == ninf ? 0.f : -m;
+          const float2 nm2 = make_float2(neg_mu, neg_mu);
+          // P goes out in two halves (keys 0-63, 64-127): the first half's stores drain through
+          // the shared-memory pipe while the second half's exponentials run.
+          exp_pack32(s0, sc2, nm2, suma, pk[0]);
+          exp_pack32(s1, sc2, nm2, suma, pk[1]);
 
           // This tile's previous P*V must be complete before its P buffer is overwritten and before
           // O is rescaled.  It is waited on every block, in order, so a parity wait is never
@@ -526,11 +522,26 @@ __global__ void __launch_bounds__(TcCfg::kThreads, 1)
             }
             tmem_wait_st();
           }
+          // P chunk u (keys 8u .. 8u + 7) of row r: K-half u / 8, chunk (u % 8) ^ (r % 8).
 #pragma unroll
-          for (int u = 0; u < 16; ++u) {
+          for (int u = 0; u < 8; ++u) {
             const int c = u >> 2, i = (u & 3) * 4;
-            st_shared_v4(p_row + (u >> 3) * 16384 + (((u & 7) ^ r7) << 4), pk[c][i], pk[c][i + 1],
+            st_shared_v4(p_row + ((u ^ r7) << 4), pk[c][i], pk[c][i + 1], pk[c][i + 2],
+                         pk[c][i + 3]);
+          }
+          exp_pack32(s2, sc2, nm2, suma, pk[2]);
+          exp_pack32(s3, sc2, nm2, suma, pk[3]);
+#pragma unroll
+          for (int u = 8; u < 16; ++u) {
+            const int c = u >> 2, i = (u & 3) * 4;
+            st_shared_v4(p_row + 16384 + (((u & 7) ^ r7) << 4), pk[c][i], pk[c][i + 1],
                          pk[c][i + 2], pk[c][i + 3]);
+          }
+          {
+            const float2 s01 = __fadd2_rn(suma[0], suma[1]);
+            const float2 s23 = __fadd2_rn(suma[2], suma[3]);
+            const float2 st = __fadd2_rn(s01, s23);
+            l = l * alpha + (st.x + st.y);
           }
           fence_proxy_async_smem();
           tc_fence_before();
