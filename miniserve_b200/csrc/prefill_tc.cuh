@@ -165,10 +165,14 @@ __device__ __forceinline__ void exp_pack32(const float (&sv)[32], float2 sc2, fl
 __global__ void __launch_bounds__(TcCfg::kThreads, 1)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap k_map,
                       const __grid_constant__ CUtensorMap v_map, const AttnArgs a) {
-  // The trigger comes after the wait: a grid launched behind this one then knows that the kernel
-  // before this one has completed (the persistent decode kernel relies on it for cascade plans).
-  pdl_wait();
-  pdl_trigger();
+  // Programmatic dependent launch.  The plan (items, sequence records, block tables) was uploaded
+  // before the kernel preceding this one started, and the K/V rows of keys below a sequence's
+  // cached length were written by earlier steps, so the producer reads the plan and streams the
+  // blocks made only of such keys before griddepcontrol.wait, while the previous kernel finishes.
+  // Everything else (the queries, this step's K/V rows, every store) comes after the wait, which
+  // every thread executes.  Each thread triggers the dependents only after its own wait: a grid
+  // launched behind this one then knows that the kernel before this one has completed (the
+  // persistent decode kernel relies on it for cascade plans).
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -254,6 +258,10 @@ __global__ void __launch_bounds__(TcCfg::kThreads, 1)
   // few registers.
   if (warp >= 8) {
     setmaxnreg_dec<TcCfg::kOtherRegs>();
+    if (warp != 8) {
+      pdl_wait();
+      pdl_trigger();
+    }
     if (warp == 8) {
       // ---------------- TMA producer ----------------
       // Position p goes to slot p % NS once every MMA that read position p - NS has finished.
@@ -264,7 +272,18 @@ __global__ void __launch_bounds__(TcCfg::kThreads, 1)
       int ids_j = (lane < 8 && lane < npages) ? table[lane] : -1;           // block j's pages
       int ids_j1 = (lane < 8 && 8 + lane < npages) ? table[8 + lane] : -1;  // block j + 1's
       int issued = 0;
+      bool waited = false;
+      auto wait_prev = [&]() {
+        if (!waited) {
+          pdl_wait();
+          pdl_trigger();
+          waited = true;
+        }
+      };
       auto load = [&](int p, bool is_v, int ids, int j) -> bool {
+        // Block j holds a key of this step (written by the previous kernel) unless all its keys
+        // are below the cached length.
+        if (key_lo + (j + 1) * TcCfg::kBlockKeys > num_cached) wait_prev();
         const int s = p % NS;
         int ok = 1;
         if (!is_v && lane < 8 && j * 8 + lane < npages &&
@@ -305,6 +324,7 @@ __global__ void __launch_bounds__(TcCfg::kThreads, 1)
           ids_j1 = (lane < 8 && (j + 2) * 8 + lane < npages) ? table[(j + 2) * 8 + lane] : -1;
         }
       }
+      wait_prev();
       // No copy may still be landing when the CTA exits: wait for the last use of each slot.
       if (lane == 0) {
         for (int p = issued > NS ? issued - NS : 0; p < issued; ++p) {
@@ -413,6 +433,8 @@ __global__ void __launch_bounds__(TcCfg::kThreads, 1)
     }
   } else {
     setmaxnreg_inc<TcCfg::kSoftmaxRegs>();
+    pdl_wait();
+    pdl_trigger();
       // Q tiles into the swizzled K-major layout: 256 rows (2 tiles x 64 tokens x 2 heads) of 16
       // chunks of 16 bytes; each load instruction of a warp covers two whole rows (512 contiguous
       // bytes: one token's two heads), so the loads coalesce.  All 16 loads are issued before any
