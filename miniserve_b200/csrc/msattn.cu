@@ -434,9 +434,15 @@ extern "C" int ms_qk_norm_rope_scatter(const void* qkv, int64_t qkv_row_stride, 
     set_error("ms_qk_norm_rope_scatter: batch too large");
     return MS_ERR_ARG;
   }
-  const cudaError_t e = launch(ms::qk_norm_rope_scatter_kernel<kWarps>,
-                               static_cast<unsigned>(blocks), kWarps * 32, 0,
-                               static_cast<cudaStream_t>(stream), a, st);
+  // The 16-byte form (two whole rows per warp instruction, half the instructions) whenever the
+  // rows and the norm weights allow 16-byte accesses; both forms give the same bits.
+  const bool v16 = aligned(qkv, 16) && aligned(q_out, 16) && qkv_row_stride % 8 == 0 &&
+                   q_out_row_stride % 8 == 0 && aligned(q_weight, 16) && aligned(k_weight, 16);
+  const cudaError_t e =
+      v16 ? launch(ms::qk_norm_rope_scatter_v16_kernel<kWarps>, static_cast<unsigned>(blocks),
+                   kWarps * 32, 0, static_cast<cudaStream_t>(stream), a, st)
+          : launch(ms::qk_norm_rope_scatter_kernel<kWarps>, static_cast<unsigned>(blocks),
+                   kWarps * 32, 0, static_cast<cudaStream_t>(stream), a, st);
   if (e != cudaSuccess) return cuda_fail("qk_norm_rope_scatter launch", e);
   return MS_OK;
 }

@@ -243,6 +243,46 @@ def test_table_positions_mode_equals_gathered_rows(cuda_device: torch.device) ->
     assert torch.equal(a["out"][rows], b["out"][rows])
 
 
+@pytest.mark.parametrize("positions_mode", [False, True], ids=["rows", "table"])
+def test_kernel_a_16_and_8_byte_forms_agree_bitwise(positions_mode: bool,
+                                                    cuda_device: torch.device) -> None:
+    """Kernel A has a 16-byte form (rows and norm weights 16-byte aligned) and an 8-byte form
+    (rows only 8-byte aligned, e.g. a qkv row stride of width + 4): the same inputs give the same
+    q and the same pool, bit for bit, through config 3's 2,048 tokens (gaussian values, so the
+    norm's sums and RoPE's products cover many binades)."""
+    from miniserve_b200.workloads import rope_tables
+
+    dev = cuda_device
+    batch = config3(seed=7)
+    t = batch.num_tokens
+    width = (H + 2 * KVH) * D
+    g = torch.Generator(device=dev).manual_seed(7)
+    qkv = torch.randn(t, width, generator=g, device=dev).mul_(3).bfloat16()
+    padded = torch.zeros(t, width + 4, dtype=torch.bfloat16, device=dev)
+    padded[:, :width] = qkv
+    qkv_v8 = padded[:, :width]  # row stride width + 4: 8-byte aligned rows only
+    assert qkv_v8.stride(0) % 8 == 4
+    qw = (1 + 0.2 * torch.randn(D, generator=g, device=dev)).bfloat16()
+    kw = (1 + 0.2 * torch.randn(D, generator=g, device=dev)).bfloat16()
+    cos_t, sin_t = rope_tables(D, batch.max_position + 8, THETA, dev)
+    pos = torch.from_numpy(batch.positions).to(dev)
+    slots = torch.from_numpy(batch.slots).to(dev)
+    if positions_mode:
+        cos, sin, pos_arg = cos_t, sin_t, pos
+    else:
+        cos, sin, pos_arg = cos_t[pos], sin_t[pos], None
+    res = []
+    for x in (qkv, qkv_v8):
+        pool, views = allocate_kv_cache(1, batch.num_blocks, KVH, dev)
+        kc, vc = views[0]
+        q = qk_norm_rope_scatter(x, qw, kw, EPS, cos, sin, slots, kc, vc, H, positions=pos_arg)
+        torch.cuda.synchronize(dev)
+        assert _capi.device_status(int(torch.cuda.current_stream(dev).cuda_stream)) == 0
+        res.append((q, pool))
+    assert torch.equal(res[0][0], res[1][0])
+    assert torch.equal(res[0][1], res[1][1])
+
+
 @pytest.mark.parametrize("strided", [False, True], ids=["contiguous", "qkv_views"])
 @pytest.mark.parametrize("name", ["mixed_bf16", "prefix_verify_bf16", "groups_bf16", "prefill_bf16"])
 def test_kv_scatter_whole_pool_bit_exact(name: str, strided: bool,
