@@ -20,9 +20,9 @@ from .attention import AttentionMetadata, _rows, _stream, attend
 from .kv_pool import HEAD_DIM, check_layer_views
 
 # Smallest step (tokens) for which ``fused_qkv="auto"`` takes kernel E: measured on a B200 against
-# cuBLAS + kernel A over 28 layers, kernel E is 0.82-0.96x from 256 to 768 tokens and 1.05-1.44x
-# from 1024 tokens up.
-FUSED_QKV_MIN_TOKENS = 1024
+# cuBLAS + kernel A (its 16-byte form) over 28 layers, kernel E is 0.74-0.93x from 64 to 1536
+# tokens, 1.01x at 2048 and 1.12-1.26x from 4096 tokens up.
+FUSED_QKV_MIN_TOKENS = 2048
 
 
 class HeadNorm(nn.Module):
