@@ -579,6 +579,9 @@ struct UnitsCfg {
   static constexpr int kGroupWarps = kConsumerWarps / kGroups;
   static constexpr int kGroupStages = kStages / kGroups;
   static_assert(kConsumerWarps % kGroups == 0 && kStages % kGroups == 0, "even split");
+  // A slot's previous fill must be a page of the same warp (the parity waits are exact only then):
+  // the group's warps take its pages in turn, so its slot count is a multiple of its warps.
+  static_assert(kGroupStages % kGroupWarps == 0, "slots per group a multiple of its warps");
   static constexpr int kThreads = (kConsumerWarps + kGroups) * 32;
   static constexpr int kStageBytes = Base::kStageBytes;
   static constexpr int kQBytes = Base::kQBytes;  // per group

@@ -13,13 +13,17 @@ This test restates the protocol as agents over mbarrier phases (TMA loads comple
 later step), runs random schedules, and checks that every page a consumer reads is the one it
 waited for and that every agent finishes.
 
-Two layouts are simulated:
-- as shipped: each group has its own producer warp and half of the ring, so within a group a
-  slot's previous fill is a page the same warp consumed (or the group's previous unit, finished
-  before the group's merge barrier);
+Three layouts are simulated:
+- as shipped: each group has its own producer warp and half of the ring (4 slots for its 2
+  warps), so within a group a slot's previous fill is a page the same warp consumed (or the
+  group's previous unit, finished before the group's merge barrier);
 - a variant that was built and not kept: both groups on one ring fed by one producer in unit
   order.  There a group can wait for a slot whose previous fill belongs to the other group and
-  has not landed yet; the simulation finds that stale read, which shows the check works.
+  has not landed yet; the simulation finds that stale read, which shows the check works;
+- per-group rings of 5 slots (considered for a deeper ring): the group's warps take its pages in
+  turn, so with an odd slot count a slot's previous fill is the other warp's page, and the
+  simulation finds the same stale read.  Hence the kernel's static_assert that the slots of a
+  group are a multiple of its warps.
 """
 
 from __future__ import annotations
@@ -62,13 +66,13 @@ class Bar:
         return (self.phase & 1) != p
 
 
-def simulate(units: list[int], per_group_rings: bool, seed: int) -> list[str]:
+def simulate(units: list[int], per_group_rings: bool, seed: int, stages: int = STAGES) -> list[str]:
     """Run one CTA over units with the given page counts; returns the violations found."""
     rng = random.Random(seed)
     errors: list[str] = []
-    full = [Bar() for _ in range(STAGES)]
-    empty = [Bar() for _ in range(STAGES)]
-    slot_page: list[object] = [None] * STAGES  # what the slot holds (a page id once loaded)
+    full = [Bar() for _ in range(stages)]
+    empty = [Bar() for _ in range(stages)]
+    slot_page: list[object] = [None] * stages  # what the slot holds (a page id once loaded)
     in_flight: list[tuple[int, object]] = []  # TMA loads issued, not yet landed: (slot, page)
 
     def group_units(g: int) -> list[int]:
@@ -76,11 +80,11 @@ def simulate(units: list[int], per_group_rings: bool, seed: int) -> list[str]:
 
     # Page ids are (unit, page); the ring sequence of a producer is its units' pages in order.
     if per_group_rings:
-        gs = STAGES // GROUPS
+        gs = stages // GROUPS
         producers = [(g, [(u, j) for u in group_units(g) for j in range(units[u])], g * gs, gs)
                      for g in range(GROUPS)]
     else:
-        producers = [(-1, [(u, j) for u in range(len(units)) for j in range(units[u])], 0, STAGES)]
+        producers = [(-1, [(u, j) for u in range(len(units)) for j in range(units[u])], 0, stages)]
 
     def producer(seq: list[tuple[int, int]], base: int, n: int):
         for g, page in enumerate(seq):
@@ -95,9 +99,9 @@ def simulate(units: list[int], per_group_rings: bool, seed: int) -> list[str]:
 
     def consumer(grp: int, gw: int):
         if per_group_rings:
-            base, n = grp * (STAGES // GROUPS), STAGES // GROUPS
+            base, n = grp * (stages // GROUPS), stages // GROUPS
         else:
-            base, n = 0, STAGES
+            base, n = 0, stages
         g0 = 0
         for u in range(len(units)):
             mine = u % GROUPS == grp
@@ -190,3 +194,14 @@ def test_shared_ring_variant_reads_stale_slots() -> None:
         if errors:
             found.append(errors[0])
     assert found, "the stale-parity read of the shared-ring variant was not found"
+
+
+def test_odd_slot_count_per_group_reads_stale_slots() -> None:
+    """5 slots per group for 2 warps: the slot of page j + 5 last held page j, the other warp's,
+    which some schedule has not landed when the first warp waits on it."""
+    found = []
+    for seed in range(40):
+        errors = simulate([12, 12, 12, 12], per_group_rings=True, seed=seed, stages=10)
+        if errors:
+            found.append(errors[0])
+    assert found, "the stale-parity read of an odd slot count was not found"
