@@ -169,111 +169,130 @@ __device__ __forceinline__ void named_bar_1_or_2(int bar_id, int threads) {
 }  // device status bits (kErr*), read by ms_device_status
 
 // Decode mode: merge the consumer warps' (m, l, O) over their page subsets through `merge`
-// (kConsumerWarps x 16 x (128 + 4) fp32 accumulators, then kConsumerWarps x 16 maxima and as many
-// sums) and write the rows: bf16 output (merged with a cascade row's shared-prefix partial when
-// merge_row >= 0) or fp32 partial rows and log2-sum-exp for split items.  Called by the
+// (kConsumerWarps x 16 x (128 / kPasses + 4) fp32 accumulators, then kConsumerWarps x 16 maxima
+// and as many sums) and write the rows: bf16 output (merged with a cascade row's shared-prefix
+// partial when merge_row >= 0) or fp32 partial rows and log2-sum-exp for split items.  With
+// kPasses = 2 the columns go through the scratch in two halves (half the shared memory, two more
+// barriers; the same values).  `pre`, when given, holds the cascade row's prefix partial already
+// copied into shared memory ([16 rows][128] O, then 16 log2-sum-exp values; the caller waited for
+// the kernel that wrote it); otherwise the partial is read from global memory.  Called by the
 // kConsumerWarps warps that attended the item (warp = 0 .. kConsumerWarps - 1 among them, tid =
 // 0 .. 32 kConsumerWarps - 1), which synchronise on named barrier bar_id.
-template <int kConsumerWarps, bool kWaitBeforeMerge = false>
+template <int kConsumerWarps, int kPasses = 1>
+__host__ __device__ constexpr int decode_merge_bytes() {
+  return kConsumerWarps * 16 * (kHeadDim / kPasses + 4) * 4 + 2 * kConsumerWarps * 16 * 4;
+}
+constexpr int kPrefixPartialBytes = 16 * kHeadDim * 4 + 16 * 4;  // one unit's [16][128] O + lse
+template <int kConsumerWarps, bool kWaitBeforeMerge = false, int kPasses = 1>
 __device__ __forceinline__ void decode_merge_store(float* merge, const float (&o)[16][4],
                                                    const float (&m)[2], const float (&l)[2],
                                                    int warp, int lane, int n_q, int kvh,
                                                    int part_row, int merge_row, int flat_start,
                                                    int tok0, const AttnArgs& a, int bar_id = 1,
-                                                   int tid = -1) {
+                                                   int tid = -1, const float* pre = nullptr) {
   if (tid < 0) tid = threadIdx.x;
+  static_assert(kPasses == 1 || kPasses == 2, "one or two column passes");
+  constexpr int kCols = kHeadDim / kPasses;  // columns per pass
+  constexpr int kChunks = kCols / 16;        // 16-column chunks per row and pass
   float* mo = merge;
-  float* mm = mo + kConsumerWarps * 16 * (kHeadDim + 4);
+  float* mm = mo + kConsumerWarps * 16 * (kCols + 4);
   float* ml = mm + kConsumerWarps * 16;
-  named_bar_1_or_2(bar_id, kConsumerWarps * 32);
-  {
-    float* wo = mo + warp * 16 * (kHeadDim + 4);
-    const int ra = lane >> 2, rb = ra + 8, c = 2 * (lane & 3);
 #pragma unroll
-    for (int n = 0; n < 16; ++n) {
-      *reinterpret_cast<float2*>(wo + ra * (kHeadDim + 4) + n * 8 + c) = make_float2(o[n][0], o[n][1]);
-      *reinterpret_cast<float2*>(wo + rb * (kHeadDim + 4) + n * 8 + c) = make_float2(o[n][2], o[n][3]);
-    }
-    if ((lane & 3) == 0) {
-      mm[warp * 16 + ra] = m[0];
-      mm[warp * 16 + rb] = m[1];
-      ml[warp * 16 + ra] = l[0];
-      ml[warp * 16 + rb] = l[1];
-    }
-  }
-  named_bar_1_or_2(bar_id, kConsumerWarps * 32);
-  for (int e = tid; e < 16 * 8; e += kConsumerWarps * 32) {
-    const int r = e >> 3;
-    const int dc = (e & 7) * 16;
-    const int tok = r >> 1;
-    if (tok >= n_q) continue;
-    float mx = -INFINITY;
+  for (int pass = 0; pass < kPasses; ++pass) {
+    named_bar_1_or_2(bar_id, kConsumerWarps * 32);  // the scratch is free
+    {
+      float* wo = mo + warp * 16 * (kCols + 4);
+      const int ra = lane >> 2, rb = ra + 8, c = 2 * (lane & 3);
 #pragma unroll
-    for (int w = 0; w < kConsumerWarps; ++w) mx = fmaxf(mx, mm[w * 16 + r]);
-    float wsc[kConsumerWarps];
-    float L = 0.f;
-#pragma unroll
-    for (int w = 0; w < kConsumerWarps; ++w) {
-      const float mw = mm[w * 16 + r];
-      wsc[w] = mw == -INFINITY ? 0.f : fast_exp2(mw - mx);
-      L += ml[w * 16 + r] * wsc[w];
-    }
-    const float invL = L > 0.f ? 1.f / L : 0.f;
-    float acc[16];
-#pragma unroll
-    for (int i = 0; i < 16; ++i) acc[i] = 0.f;
-#pragma unroll
-    for (int w = 0; w < kConsumerWarps; ++w) {
-      const float* src = mo + (w * 16 + r) * (kHeadDim + 4) + dc;
-#pragma unroll
-      for (int i = 0; i < 16; ++i) acc[i] += src[i] * wsc[w];
-    }
-    const int head = kvh * kGroup + (r & 1);
-    if (part_row < 0) {
-      __nv_bfloat16* dst = a.out + static_cast<long long>(flat_start + tok0 + tok) * a.out_row_stride +
-                           head * kHeadDim + dc;
-      float scale_u = invL;  // weight of this item's own (unnormalised) accumulator
-      float wp = 0.f;        // weight of the merged shared-prefix partial
-      const float* op = nullptr;
-      if (merge_row >= 0) {
-        // Cascade row: merge the shared-prefix partial (normalised O and log2-sum-exp) that the
-        // tensor-core kernel wrote before this launch: out = (acc 2^(mx-M) + O_p L_p') / (...).
-        if constexpr (kWaitBeforeMerge) pdl_wait();  // the partial is that kernel's output
-        const long long prow = static_cast<long long>(merge_row + r) * a.num_kv + kvh;
-        const float lse_p = a.ws_lse[prow];
-        const float lse_u = L > 0.f ? mx + __log2f(L) : -INFINITY;
-        const float M = fmaxf(lse_u, lse_p);
-        const float wu = lse_u == -INFINITY ? 0.f : fast_exp2(lse_u - M);
-        wp = lse_p == -INFINITY ? 0.f : fast_exp2(lse_p - M);
-        const float inv = wu + wp > 0.f ? 1.f / (wu + wp) : 0.f;
-        scale_u = invL * wu * inv;
-        wp *= inv;
-        op = a.ws_o + prow * kHeadDim + dc;
+      for (int nn = 0; nn < 16 / kPasses; ++nn) {
+        const int n = pass * (16 / kPasses) + nn;
+        *reinterpret_cast<float2*>(wo + ra * (kCols + 4) + nn * 8 + c) = make_float2(o[n][0], o[n][1]);
+        *reinterpret_cast<float2*>(wo + rb * (kCols + 4) + nn * 8 + c) = make_float2(o[n][2], o[n][3]);
       }
-      if (op != nullptr) {
+      if (pass == 0 && (lane & 3) == 0) {
+        mm[warp * 16 + ra] = m[0];
+        mm[warp * 16 + rb] = m[1];
+        ml[warp * 16 + ra] = l[0];
+        ml[warp * 16 + rb] = l[1];
+      }
+    }
+    named_bar_1_or_2(bar_id, kConsumerWarps * 32);
+    for (int e = tid; e < 16 * kChunks; e += kConsumerWarps * 32) {
+      const int r = e / kChunks;
+      const int dcl = (e % kChunks) * 16;  // column inside the pass
+      const int dc = pass * kCols + dcl;
+      const int tok = r >> 1;
+      if (tok >= n_q) continue;
+      float mx = -INFINITY;
 #pragma unroll
-        for (int i = 0; i < 16; i += 4) {
-          const float4 pv = *reinterpret_cast<const float4*>(op + i);
-          acc[i] = acc[i] * scale_u + pv.x * wp;
-          acc[i + 1] = acc[i + 1] * scale_u + pv.y * wp;
-          acc[i + 2] = acc[i + 2] * scale_u + pv.z * wp;
-          acc[i + 3] = acc[i + 3] * scale_u + pv.w * wp;
+      for (int w = 0; w < kConsumerWarps; ++w) mx = fmaxf(mx, mm[w * 16 + r]);
+      float wsc[kConsumerWarps];
+      float L = 0.f;
+#pragma unroll
+      for (int w = 0; w < kConsumerWarps; ++w) {
+        const float mw = mm[w * 16 + r];
+        wsc[w] = mw == -INFINITY ? 0.f : fast_exp2(mw - mx);
+        L += ml[w * 16 + r] * wsc[w];
+      }
+      const float invL = L > 0.f ? 1.f / L : 0.f;
+      float acc[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) acc[i] = 0.f;
+#pragma unroll
+      for (int w = 0; w < kConsumerWarps; ++w) {
+        const float* src = mo + (w * 16 + r) * (kCols + 4) + dcl;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) acc[i] += src[i] * wsc[w];
+      }
+      const int head = kvh * kGroup + (r & 1);
+      if (part_row < 0) {
+        __nv_bfloat16* dst = a.out + static_cast<long long>(flat_start + tok0 + tok) * a.out_row_stride +
+                             head * kHeadDim + dc;
+        float scale_u = invL;  // weight of this item's own (unnormalised) accumulator
+        float wp = 0.f;        // weight of the merged shared-prefix partial
+        const float* op = nullptr;
+        if (merge_row >= 0) {
+          // Cascade row: merge the shared-prefix partial (normalised O and log2-sum-exp) that the
+          // tensor-core kernel wrote before this launch: out = (acc 2^(mx-M) + O_p L_p') / (...).
+          const long long prow = static_cast<long long>(merge_row + r) * a.num_kv + kvh;
+          if constexpr (kWaitBeforeMerge) {
+            if (pre == nullptr) pdl_wait();  // the partial is that kernel's output
+          }
+          const float lse_p = pre != nullptr ? pre[16 * kHeadDim + r] : a.ws_lse[prow];
+          const float lse_u = L > 0.f ? mx + __log2f(L) : -INFINITY;
+          const float M = fmaxf(lse_u, lse_p);
+          const float wu = lse_u == -INFINITY ? 0.f : fast_exp2(lse_u - M);
+          wp = lse_p == -INFINITY ? 0.f : fast_exp2(lse_p - M);
+          const float inv = wu + wp > 0.f ? 1.f / (wu + wp) : 0.f;
+          scale_u = invL * wu * inv;
+          wp *= inv;
+          op = pre != nullptr ? pre + r * kHeadDim + dc : a.ws_o + prow * kHeadDim + dc;
         }
-        scale_u = 1.f;
+        if (op != nullptr) {
+#pragma unroll
+          for (int i = 0; i < 16; i += 4) {
+            const float4 pv = *reinterpret_cast<const float4*>(op + i);
+            acc[i] = acc[i] * scale_u + pv.x * wp;
+            acc[i + 1] = acc[i + 1] * scale_u + pv.y * wp;
+            acc[i + 2] = acc[i + 2] * scale_u + pv.z * wp;
+            acc[i + 3] = acc[i + 3] * scale_u + pv.w * wp;
+          }
+          scale_u = 1.f;
+        }
+        uint32_t pk[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) pk[i] = pack_bf16(acc[2 * i] * scale_u, acc[2 * i + 1] * scale_u);
+        reinterpret_cast<uint4*>(dst)[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        reinterpret_cast<uint4*>(dst)[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+      } else {
+        const long long prow = static_cast<long long>(part_row + r) * a.num_kv + kvh;
+        float* dst = a.ws_o + prow * kHeadDim + dc;
+#pragma unroll
+        for (int i = 0; i < 16; i += 4)
+          *reinterpret_cast<float4*>(dst + i) =
+              make_float4(acc[i] * invL, acc[i + 1] * invL, acc[i + 2] * invL, acc[i + 3] * invL);
+        if (dc == 0) a.ws_lse[prow] = L > 0.f ? mx + __log2f(L) : -INFINITY;
       }
-      uint32_t pk[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) pk[i] = pack_bf16(acc[2 * i] * scale_u, acc[2 * i + 1] * scale_u);
-      reinterpret_cast<uint4*>(dst)[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-      reinterpret_cast<uint4*>(dst)[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
-    } else {
-      const long long prow = static_cast<long long>(part_row + r) * a.num_kv + kvh;
-      float* dst = a.ws_o + prow * kHeadDim + dc;
-#pragma unroll
-      for (int i = 0; i < 16; i += 4)
-        *reinterpret_cast<float4*>(dst + i) =
-            make_float4(acc[i] * invL, acc[i + 1] * invL, acc[i + 2] * invL, acc[i + 3] * invL);
-      if (dc == 0) a.ws_lse[prow] = L > 0.f ? mx + __log2f(L) : -INFINITY;
     }
   }
 }
@@ -586,8 +605,11 @@ struct UnitsCfg {
   static constexpr int kStageBytes = Base::kStageBytes;
   static constexpr int kQBytes = Base::kQBytes;  // per group
   static constexpr int kMergeOff = kStageBytes + kGroups * kQBytes;
-  static constexpr int kGroupMergeBytes =
-      kGroupWarps * 16 * (kHeadDim + 4) * 4 + 2 * kGroupWarps * 16 * 4;  // per group
+  // Per group: the merge scratch (the merge goes through it in two column passes) and a buffer
+  // for the unit's shared-prefix partial, copied in while the unit's pages stream.
+  static constexpr int kGroupScratchBytes = decode_merge_bytes<kGroupWarps, 2>();
+  static constexpr int kGroupMergeBytes = kGroupScratchBytes + kPrefixPartialBytes;
+  static_assert(kGroupScratchBytes % 16 == 0, "16-byte aligned partial buffer");
   static constexpr int kMergeBytes = kGroups * kGroupMergeBytes;
   static constexpr int kBarOffset = kMergeOff + kMergeBytes;
   static constexpr int kSmemBytes = 1024 + kBarOffset + 2 * kStages * 8 + 16;
@@ -746,6 +768,10 @@ __global__ void __launch_bounds__(UnitsCfg<kConsumerWarps, kStages>::kThreads, 2
   uint64_t* gfull = full + grp * kGS;
   uint64_t* gempty = empty + grp * kGS;
   float* merge_g = merge + grp * (Cfg::kGroupMergeBytes / 4);
+  float* partial_g = merge_g + Cfg::kGroupScratchBytes / 4;
+  // Whether the kernel that writes the shared-prefix partials is known to have completed (this
+  // thread has executed griddepcontrol.wait): from the start unless this launch overlaps it.
+  bool partials_ready = !kAfterPrefix;
   int g0 = 0;  // this unit's first page in the group's ring sequence
   for (int u = u_first; u < n_units; u += ustep) {
     const int item_idx = u / a.num_kv;
@@ -773,6 +799,29 @@ __global__ void __launch_bounds__(UnitsCfg<kConsumerWarps, kStages>::kThreads, 2
     }
     // Every warp of the group holds its query fragments: the tile takes the next unit's rows.
     named_bar_1_or_2(bar_id, kGW * 32);
+    // A cascade row's shared-prefix partial (rows r < 2 n_q: 128 fp32 of O and the log2-sum-exp)
+    // is copied into the group's buffer while the unit's pages stream, so the merge reads it
+    // from shared memory.
+    const bool cascade_row = part_row < 0 && merge_row >= 0;
+    const bool pre = partials_ready && cascade_row;
+    if (pre) {
+      const uint32_t pbase = smem_u32(partial_g);
+      for (int c = gtid; c < 2 * n_q * 32; c += kGW * 32) {
+        const int r = c >> 5, ch = c & 31;
+        const float* src =
+            a.ws_o + (static_cast<long long>(merge_row + r) * a.num_kv + kvh) * kHeadDim + ch * 4;
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(pbase + r * 512 + ch * 16),
+                     "l"(src)
+                     : "memory");
+      }
+      if (gtid < 2 * n_q) {
+        const float* src = a.ws_lse + static_cast<long long>(merge_row + gtid) * a.num_kv + kvh;
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(pbase + 16 * kHeadDim * 4 + gtid * 4),
+                     "l"(src)
+                     : "memory");
+      }
+      asm volatile("cp.async.commit_group;" ::: "memory");
+    }
     if (u + ustep < n_units) prefetch_q(u + ustep);
 
     float o[16][4];
@@ -813,8 +862,21 @@ __global__ void __launch_bounds__(UnitsCfg<kConsumerWarps, kStages>::kThreads, 2
       l[i] += __shfl_xor_sync(0xffffffffu, l[i], 1);
       l[i] += __shfl_xor_sync(0xffffffffu, l[i], 2);
     }
-    decode_merge_store<kGW, kAfterPrefix>(merge_g, o, m, l, gw, lane, n_q, kvh, part_row,
-                                          merge_row, flat_start, tok0, a, bar_id, gtid);
+    if (pre) {  // this thread's copies of the partial (not the next query tile's) have landed
+      if (u + ustep < n_units)
+        asm volatile("cp.async.wait_group 1;" ::: "memory");
+      else
+        asm volatile("cp.async.wait_group 0;" ::: "memory");
+    }
+    decode_merge_store<kGW, kAfterPrefix, 2>(merge_g, o, m, l, gw, lane, n_q, kvh, part_row,
+                                             merge_row, flat_start, tok0, a, bar_id, gtid,
+                                             pre ? partial_g : nullptr);
+    if (cascade_row && !partials_ready) {
+      // The merge waited for that kernel only in the threads that read a partial row; every
+      // thread copies the next units' partials, so every thread waits (at once, by now).
+      if constexpr (kAfterPrefix) pdl_wait();
+      partials_ready = true;
+    }
     g0 += npages;
   }
   if constexpr (kAfterPrefix) pdl_wait();
