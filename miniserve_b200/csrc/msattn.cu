@@ -699,10 +699,20 @@ extern "C" int ms_paged_attention(const void* q, int64_t q_row_stride, void* out
       // Many short items: two persistent CTAs per SM walk the work units.  Right after the
       // tensor-core kernel of a cascade plan they also overlap its last wave.
       const bool after_prefix = plan->n_cascade > 0 && plan->n_tc_items > 0 && ds == s;
+      // When the tensor-core kernel ends in a small partial wave (e.g. 160 CTAs on 148 SMs), the
+      // CTAs placed on the SMs that wave holds start one tensor-core CTA later than the rest but
+      // get the same share of the units (a static stride), so they finish last (config 4: 24
+      // CTAs ending at 83-88 us against 74 us for the rest).  Those SMs are left out of the grid.
+      int grid = 2 * sms;
+      if (after_prefix) {
+        const int64_t tc_ctas = static_cast<int64_t>(plan->n_tc_items) * num_kv_heads;
+        const int rem = static_cast<int>(tc_ctas % sms);
+        if (tc_ctas > sms && rem > 0 && rem <= sms / 8) grid = 2 * (sms - rem);
+      }
       e = after_prefix
-              ? launch(ms::paged_decode_units_kernel<kDecodeWarps, kDecodeStages, true>, 2 * sms,
+              ? launch(ms::paged_decode_units_kernel<kDecodeWarps, kDecodeStages, true>, grid,
                        UnitsCfg::kThreads, UnitsCfg::kSmemBytes, ds, map, a)
-              : launch(ms::paged_decode_units_kernel<kDecodeWarps, kDecodeStages>, 2 * sms,
+              : launch(ms::paged_decode_units_kernel<kDecodeWarps, kDecodeStages>, grid,
                        UnitsCfg::kThreads, UnitsCfg::kSmemBytes, ds, map, a);
     } else {
       e = launch(ms::paged_attn_kernel<0, kDecodeWarps, kDecodeStages>, ctas,

@@ -175,7 +175,9 @@ __device__ __forceinline__ void named_bar_1_or_2(int bar_id, int threads) {
 // kPasses = 2 the columns go through the scratch in two halves (half the shared memory, two more
 // barriers; the same values).  `pre`, when given, holds the cascade row's prefix partial already
 // copied into shared memory ([16 rows][128] O, then 16 log2-sum-exp values; the caller waited for
-// the kernel that wrote it); otherwise the partial is read from global memory.  Called by the
+// the kernel that wrote it); otherwise the partial is read from global memory.  `park`, when
+// given, receives a cascade row's own result in that layout (normalised O and log2-sum-exp)
+// instead of the output, to be merged with the prefix partial later (finish_parked).  Called by the
 // kConsumerWarps warps that attended the item (warp = 0 .. kConsumerWarps - 1 among them, tid =
 // 0 .. 32 kConsumerWarps - 1), which synchronise on named barrier bar_id.
 template <int kConsumerWarps, int kPasses = 1>
@@ -189,7 +191,8 @@ __device__ __forceinline__ void decode_merge_store(float* merge, const float (&o
                                                    int warp, int lane, int n_q, int kvh,
                                                    int part_row, int merge_row, int flat_start,
                                                    int tok0, const AttnArgs& a, int bar_id = 1,
-                                                   int tid = -1, const float* pre = nullptr) {
+                                                   int tid = -1, const float* pre = nullptr,
+                                                   float* park = nullptr) {
   if (tid < 0) tid = threadIdx.x;
   static_assert(kPasses == 1 || kPasses == 2, "one or two column passes");
   constexpr int kCols = kHeadDim / kPasses;  // columns per pass
@@ -245,7 +248,13 @@ __device__ __forceinline__ void decode_merge_store(float* merge, const float (&o
         for (int i = 0; i < 16; ++i) acc[i] += src[i] * wsc[w];
       }
       const int head = kvh * kGroup + (r & 1);
-      if (part_row < 0) {
+      if (park != nullptr) {
+#pragma unroll
+        for (int i = 0; i < 16; i += 4)
+          *reinterpret_cast<float4*>(park + r * kHeadDim + dc + i) =
+              make_float4(acc[i] * invL, acc[i + 1] * invL, acc[i + 2] * invL, acc[i + 3] * invL);
+        if (dc == 0) park[16 * kHeadDim + r] = L > 0.f ? mx + __log2f(L) : -INFINITY;
+      } else if (part_row < 0) {
         __nv_bfloat16* dst = a.out + static_cast<long long>(flat_start + tok0 + tok) * a.out_row_stride +
                              head * kHeadDim + dc;
         float scale_u = invL;  // weight of this item's own (unnormalised) accumulator
@@ -294,6 +303,46 @@ __device__ __forceinline__ void decode_merge_store(float* merge, const float (&o
         if (dc == 0) a.ws_lse[prow] = L > 0.f ? mx + __log2f(L) : -INFINITY;
       }
     }
+  }
+}
+
+// A parked cascade row (decode_merge_store's `park`): out = (O_u 2^(lse_u - M) + O_p 2^(lse_p - M))
+// / (2^(lse_u - M) + 2^(lse_p - M)) with the shared-prefix partial (O_p, lse_p) read from global
+// memory; the caller has waited for the kernel that wrote it, and the parked rows were written
+// before a barrier of the same threads.  kT threads (tid = 0 .. kT - 1) share the 16 x 8 chunks.
+template <int kT>
+__device__ __forceinline__ void finish_parked(const float* park, int n_q, int kvh, int merge_row,
+                                              int flat_start, int tok0, const AttnArgs& a,
+                                              int tid) {
+  for (int e = tid; e < 16 * 8; e += kT) {
+    const int r = e >> 3;
+    const int dc = (e & 7) * 16;
+    const int tok = r >> 1;
+    if (tok >= n_q) continue;
+    const long long prow = static_cast<long long>(merge_row + r) * a.num_kv + kvh;
+    const float lse_p = a.ws_lse[prow];
+    const float lse_u = park[16 * kHeadDim + r];
+    const float M = fmaxf(lse_u, lse_p);
+    float wu = lse_u == -INFINITY ? 0.f : fast_exp2(lse_u - M);
+    float wp = lse_p == -INFINITY ? 0.f : fast_exp2(lse_p - M);
+    const float inv = wu + wp > 0.f ? 1.f / (wu + wp) : 0.f;
+    wu *= inv;
+    wp *= inv;
+    const float* ou = park + r * kHeadDim + dc;
+    const float* op = a.ws_o + prow * kHeadDim + dc;
+    uint32_t pk[8];
+#pragma unroll
+    for (int i = 0; i < 16; i += 4) {
+      const float4 u4 = *reinterpret_cast<const float4*>(ou + i);
+      const float4 p4 = *reinterpret_cast<const float4*>(op + i);
+      pk[i / 2] = pack_bf16(u4.x * wu + p4.x * wp, u4.y * wu + p4.y * wp);
+      pk[i / 2 + 1] = pack_bf16(u4.z * wu + p4.z * wp, u4.w * wu + p4.w * wp);
+    }
+    const int head = kvh * kGroup + (r & 1);
+    __nv_bfloat16* dst =
+        a.out + static_cast<long long>(flat_start + tok0 + tok) * a.out_row_stride + head * kHeadDim + dc;
+    reinterpret_cast<uint4*>(dst)[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+    reinterpret_cast<uint4*>(dst)[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
   }
 }
 
@@ -772,6 +821,11 @@ __global__ void __launch_bounds__(UnitsCfg<kConsumerWarps, kStages>::kThreads, 2
   // Whether the kernel that writes the shared-prefix partials is known to have completed (this
   // thread has executed griddepcontrol.wait): from the start unless this launch overlaps it.
   bool partials_ready = !kAfterPrefix;
+  // A group's first cascade unit does not wait for that kernel: its own result is parked in the
+  // partial buffer and merged with the prefix partial at the group's next merge, by which time
+  // that kernel has normally completed, so the group keeps streaming pages meanwhile.
+  bool parked = false;
+  int pk_n_q = 0, pk_kvh = 0, pk_merge_row = 0, pk_flat = 0, pk_tok0 = 0;
   int g0 = 0;  // this unit's first page in the group's ring sequence
   for (int u = u_first; u < n_units; u += ustep) {
     const int item_idx = u / a.num_kv;
@@ -868,10 +922,26 @@ __global__ void __launch_bounds__(UnitsCfg<kConsumerWarps, kStages>::kThreads, 2
       else
         asm volatile("cp.async.wait_group 0;" ::: "memory");
     }
+    const bool park_now =
+        kAfterPrefix && cascade_row && !partials_ready && !parked && u + ustep < n_units;
+    if (parked) {
+      pdl_wait();  // returns once the kernel that writes the prefix partials has completed
+      finish_parked<kGW * 32>(partial_g, pk_n_q, pk_kvh, pk_merge_row, pk_flat, pk_tok0, a, gtid);
+      parked = false;
+      partials_ready = true;
+    }
     decode_merge_store<kGW, kAfterPrefix, 2>(merge_g, o, m, l, gw, lane, n_q, kvh, part_row,
                                              merge_row, flat_start, tok0, a, bar_id, gtid,
-                                             pre ? partial_g : nullptr);
-    if (cascade_row && !partials_ready) {
+                                             pre ? partial_g : nullptr,
+                                             park_now ? partial_g : nullptr);
+    if (park_now) {
+      parked = true;
+      pk_n_q = n_q;
+      pk_kvh = kvh;
+      pk_merge_row = merge_row;
+      pk_flat = flat_start;
+      pk_tok0 = tok0;
+    } else if (cascade_row && !partials_ready) {
       // The merge waited for that kernel only in the threads that read a partial row; every
       // thread copies the next units' partials, so every thread waits (at once, by now).
       if constexpr (kAfterPrefix) pdl_wait();
@@ -879,7 +949,12 @@ __global__ void __launch_bounds__(UnitsCfg<kConsumerWarps, kStages>::kThreads, 2
     }
     g0 += npages;
   }
-  if constexpr (kAfterPrefix) pdl_wait();
+  if constexpr (kAfterPrefix) {
+    pdl_wait();
+    // A unit parked by a group whose loop then ended early (a timeout) is still written out.
+    if (parked)
+      finish_parked<kGW * 32>(partial_g, pk_n_q, pk_kvh, pk_merge_row, pk_flat, pk_tok0, a, gtid);
+  }
 }
 
 struct CombineArgs {
