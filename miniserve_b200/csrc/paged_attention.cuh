@@ -788,12 +788,10 @@ __global__ void __launch_bounds__(UnitsCfg<kConsumerWarps, kStages>::kThreads, 2
   constexpr int kPer = 16 * 16 / (kGW * 32);
   static_assert(16 * 16 % (kGW * 32) == 0, "query chunks per thread");
   const uint32_t qbase_s = smem_u32(qtile + grp * Cfg::kQBytes);
-  auto prefetch_q = [&](int u) {
-    const int item_idx = u / a.num_kv;
-    const int kvh = u - item_idx * a.num_kv;
-    const int* it = a.items + static_cast<long long>(item_idx) * kRec;
-    const int tok0 = it[1], n_q = it[2];
-    const int flat_start = a.seqs[static_cast<long long>(it[0]) * kRec];
+  // Unit u's query rows from its item fields (token offset, token count, the sequence's first
+  // flat row), which the caller loaded a unit ahead, so no dependent global load stalls here.
+  auto prefetch_q = [&](int u, int tok0, int n_q, int flat_start) {
+    const int kvh = u % a.num_kv;
 #pragma unroll
     for (int k = 0; k < kPer; ++k) {
       const int c = gtid + k * kGW * 32;
@@ -811,8 +809,27 @@ __global__ void __launch_bounds__(UnitsCfg<kConsumerWarps, kStages>::kThreads, 2
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
   };
+  // The item fields of a unit: token offset, token count and sequence (for its first flat row).
+  auto unit_fields = [&](int u, int& tok0, int& n_q, int& seq) {
+    const int* it = a.items + static_cast<long long>(u / a.num_kv) * kRec;
+    seq = it[0];
+    tok0 = it[1];
+    n_q = it[2];
+  };
   const int u_first = static_cast<int>(blockIdx.x) + grp * static_cast<int>(gridDim.x);
-  if (u_first < n_units) prefetch_q(u_first);
+  // Fields of the group's next unit (u + ustep): its query tile is copied at the start of unit
+  // u.  Its token offset and count are loaded at the start of the unit before, and its sequence's
+  // first flat row after that unit's page loop (it depends on the sequence id).
+  int nx_tok0 = 0, nx_nq = 0, nx_seq = 0, nx_flat = 0;
+  if (u_first < n_units) {
+    int t0, nq, sq;
+    unit_fields(u_first, t0, nq, sq);
+    prefetch_q(u_first, t0, nq, a.seqs[static_cast<long long>(sq) * kRec]);
+    if (u_first + ustep < n_units) {
+      unit_fields(u_first + ustep, nx_tok0, nx_nq, nx_seq);
+      nx_flat = a.seqs[static_cast<long long>(nx_seq) * kRec];
+    }
+  }
   const uint32_t ring_u32 = smem_u32(ring + grp * kGS * kPageKVBytes);
   uint64_t* gfull = full + grp * kGS;
   uint64_t* gempty = empty + grp * kGS;
@@ -876,7 +893,10 @@ __global__ void __launch_bounds__(UnitsCfg<kConsumerWarps, kStages>::kThreads, 2
       }
       asm volatile("cp.async.commit_group;" ::: "memory");
     }
-    if (u + ustep < n_units) prefetch_q(u + ustep);
+    if (u + ustep < n_units) prefetch_q(u + ustep, nx_tok0, nx_nq, nx_flat);
+    // The unit after next: its fields are loaded now and land during this unit's page loop.
+    const bool has_next2 = u + 2 * ustep < n_units;
+    if (has_next2) unit_fields(u + 2 * ustep, nx_tok0, nx_nq, nx_seq);
 
     float o[16][4];
 #pragma unroll
@@ -916,6 +936,8 @@ __global__ void __launch_bounds__(UnitsCfg<kConsumerWarps, kStages>::kThreads, 2
       l[i] += __shfl_xor_sync(0xffffffffu, l[i], 1);
       l[i] += __shfl_xor_sync(0xffffffffu, l[i], 2);
     }
+    // Its sequence's first flat row lands during the merge.
+    if (has_next2) nx_flat = a.seqs[static_cast<long long>(nx_seq) * kRec];
     if (pre) {  // this thread's copies of the partial (not the next query tile's) have landed
       if (u + ustep < n_units)
         asm volatile("cp.async.wait_group 1;" ::: "memory");
