@@ -222,6 +222,41 @@ def test_cascade_group_beside_other_rows(cuda_device: torch.device) -> None:
     assert err <= ATOL, err
 
 
+def test_cascade_group_with_unrelated_rows_on_the_persistent_decode_kernel(
+        cuda_device: torch.device) -> None:
+    """Config 4's 512-row group (its prefix on 160 tensor-core CTAs: a small second wave, so the
+    persistent decode kernel leaves those SMs out of its grid) between 64 unrelated decode and
+    verify rows.  The decode kernel follows the tensor-core kernel and walks both kinds of unit;
+    the unrelated rows have more pages, so they come first and many consumer groups start with a
+    unit that merges no prefix before the unit they park.  Every row against the fp32 oracle."""
+    import numpy as np
+
+    rng = np.random.default_rng(16)
+    g = config4(seed=16, num_seqs=512)
+    other = [(int(rng.choice([1, 1, 5])), int(rng.integers(100, 600))) for _ in range(64)]
+    rows = other[:32] + [(c.num_new, c.num_cached) for c in g.chunks] + other[32:]
+    batch = custom(rows, seed=17)
+    chunks = list(batch.chunks)
+    lo, hi = 32, 32 + 512
+    prefix = list(chunks[lo].block_table[:64])
+    for i in range(lo, hi):
+        c = chunks[i]
+        chunks[i] = type(c)(c.flat_start, c.num_new, c.num_cached, prefix + list(c.block_table[64:]))
+    shared = Batch(batch.name, chunks, batch.num_blocks, 0)
+    inp = random_inputs(shared, 17)
+    got = run_layer(inp, cuda_device)
+    assert int(got["status"]) == 0
+    info = got["meta_info"]
+    assert info.n_cascade == 1
+    assert 148 < info.n_tc_items * KVH <= 148 + 148 // 8  # a small second tensor-core wave
+    assert info.n_decode_items * KVH > 2 * 148  # more than one resident decode wave
+    assert info.decode_pages <= 32 * info.n_decode_items  # ... of short items: the units kernel
+    rows_ = covered_rows(inp)
+    ref32 = _fp32_reference_out(inp, got["q_rot"], got["k_slots"], got["v_slots"])[rows_]
+    err = (got["out"].cpu()[rows_].float() - ref32).abs().max().item()
+    assert err <= ATOL, err
+
+
 @pytest.mark.parametrize("name", ["mixed_bf16", "prefix_verify_bf16", "prefill_bf16"])
 def test_scatter_only_path_equals_fused(name: str, cuda_device: torch.device) -> None:
     """paged_attention(q, k, v, ...) (reference call shape) == the fused layer path."""
