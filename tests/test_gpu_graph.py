@@ -20,15 +20,19 @@ from miniserve_b200.workloads import config2, config3, config4, rope_tables
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("workload", ["config2_32rows", "config3", "config4_64rows"])
+@pytest.mark.parametrize("workload", ["config2_32rows", "config3", "config4_64rows", "config4"])
 def test_graph_replay_matches_eager(workload: str, cuda_device: torch.device) -> None:
     """Decode rows with forced splits (kernels A, B, C), config 3's chunks (kernel D beside the
-    decode kernel) and a cascade group (kernel D's prefix partials merged by kernel B)."""
+    decode kernel), a 64-row cascade group (kernel D's prefix partials merged by the persistent
+    decode kernel beside kernel D's one wave) and config 4's 512-row group (kernel D's small
+    second wave: the decode grid leaves its SMs out, and consumer groups park their first unit)."""
     dev = cuda_device
     if workload == "config2_32rows":
         layers, batch, split = 28, config2(seed=5, num_seqs=32), 16
     elif workload == "config3":
         layers, batch, split = 4, config3(seed=5), 0
+    elif workload == "config4":
+        layers, batch, split = 2, config4(seed=5, num_seqs=512), 0
     else:
         layers, batch, split = 4, config4(seed=5, num_seqs=64), 0
     t = batch.num_tokens
