@@ -630,10 +630,13 @@ __global__ void __launch_bounds__(AttnCfg<kMode, kConsumerWarps, kStages>::kThre
 }
 
 // Decode mode, persistent over work units (unit u = (item u / num_kv, KV head u % num_kv); CTA c
-// takes units c, c + G, c + 2G, ...) for plans of many short items, where a one-unit CTA spends
-// most of its life starting up and finishing: here the producers stream the next units' pages
-// while the consumers finish the current ones, and each unit's query rows are copied into shared
-// memory during the group's previous unit.  Per unit the consumer work is kernel B's decode mode
+// takes units c, c + G, c + 2G, ..., G = gridDim.x, alternately for its two consumer groups) for
+// plans of many short items, where a one-unit CTA spends most of its life starting up and
+// finishing: here the producers stream the next units' pages while the consumers finish the
+// current ones, and each unit's query rows are copied into shared memory during the group's
+// previous unit (from item fields loaded a unit earlier still).  The launcher may give the grid
+// fewer than two CTAs per SM (it leaves out the SMs held by the previous kernel's small last
+// wave); nothing here depends on the grid size.  Per unit the consumer work is kernel B's decode mode
 // (the same attend_page and decode_merge_store) with the unit's pages split over the group's
 // warps instead of all consumer warps, so the results equal kernel B's up to the order in which
 // the per-warp partial sums are merged; the merge scratch has its own shared memory because the
@@ -669,8 +672,10 @@ struct UnitsCfg {
 // its own wait has returned, so when this grid starts the kernel before it (which wrote the
 // queries and this step's K/V rows) has completed: everything except the shared-prefix partials
 // may be read at once, and the page loops run during the tensor-core kernel's last wave.  The
-// prefix partials are read after pdl_wait(), and every thread waits before it exits, so this
-// grid never completes before the tensor-core kernel (later kernels rely on that ordering).
+// prefix partials are read after pdl_wait() (a consumer group parks its first cascade unit's own
+// result and merges it at its next merge, after the wait, instead of waiting at once), and every
+// thread waits before it exits, so this grid never completes before the tensor-core kernel
+// (later kernels rely on that ordering).
 template <int kConsumerWarps, int kStages, bool kAfterPrefix = false>
 __global__ void __launch_bounds__(UnitsCfg<kConsumerWarps, kStages>::kThreads, 2)
     paged_decode_units_kernel(const __grid_constant__ CUtensorMap kv_map, const AttnArgs a) {
