@@ -367,13 +367,22 @@ __global__ void __launch_bounds__(TcCfg::kThreads, 1)
             // S_t(j) = Q_t K_j^T into tile t's S columns, as soon as tile t holds S_t(j-1) in
             // registers and K_j has landed (and, for S(0), Q is stored).  The tiles are not coupled:
             // each goes as soon as its own softmax has released its S columns.
+            // The ring's full barriers are waited on by parity, which is exact only while the
+            // slot's previous fill has completed.  K_j's slot last held V_{j-3} (K_2's held K_0,
+            // which this thread waited for): K_j is waited on after the first tile's s_free(j - 1),
+            // which that tile's softmax arrives on after its wait for P*V(j - 3), so V_{j-3} had
+            // landed.
             ok = nblk == 0 || mbar_wait_mma(q_ready, 0, abort_flag);
             for (int j = 0; ok && j < nblk; ++j) {
-              if (!(ok = wait_slot(pos_k(j)))) break;
               const uint64_t kd = dk + (pos_k(j) % NS) * kSlot16;
+              bool k_landed = false;
               for (int t = 0; ok && t < 2; ++t) {
                 if (j < nblk_t[t]) {
                   if (j > 0 && !(ok = mbar_wait_mma(&s_free[t], (j - 1) & 1, abort_flag))) break;
+                  if (!k_landed) {
+                    if (!(ok = wait_slot(pos_k(j)))) break;
+                    k_landed = true;
+                  }
                   tc_fence_after();
                   const uint64_t qd = dq + t * (TcCfg::kQBytes >> 4);
 #pragma unroll
@@ -392,15 +401,22 @@ __global__ void __launch_bounds__(TcCfg::kThreads, 1)
             // the tiles go in the order their P becomes ready, so a tile whose softmax runs late
             // (its diagonal block, or its epilogue beside the other tile) does not hold the other
             // tile's P*V back.  Each tile's p_full phase is j: it takes part in entries 0 .. n - 1.
+            // V_j's slot last held K_j (the last block's, V_{j-2}, which this thread waited for),
+            // so V_j is waited on (by parity, exact only once that fill has completed) after the
+            // first P(j) is ready: P(j) follows S(j), which read K_j.
             for (int j = 0; ok && j < nblk; ++j) {
-              if (!(ok = wait_slot(pos_v(j)))) break;
               const uint64_t vd = dv + (pos_v(j) % NS) * kSlot16;
+              bool v_landed = false;
               int pend = (j < nblk_t[0] ? 1 : 0) | (j < nblk_t[1] ? 2 : 0);
               for (int i = 0; pend != 0; ++i) {
                 const int t = ((pend & 1) && mbar_test_wait(&p_full[0], j & 1))   ? 0
                               : ((pend & 2) && mbar_test_wait(&p_full[1], j & 1)) ? 1
                                                                                   : -1;
                 if (t >= 0) {
+                  if (!v_landed) {
+                    if (!(ok = wait_slot(pos_v(j)))) break;
+                    v_landed = true;
+                  }
                   tc_fence_after();
 #pragma unroll
                   for (int kk = 0; kk < 8; ++kk)
