@@ -226,7 +226,8 @@ extern "C" int ms_plan_build(int32_t num_seqs, const int32_t* flat_start, const 
       // without tensor-core work, split just those, into pieces of about that size (60 rows of
       // 100 tokens + 4 of 4000: 77.0 -> 25.2 us).  Beside tensor-core work the decode launch
       // overlaps it on a second stream and a combine pass would wait for both: config 3 measured
-      // 77.4 -> 84.6 us per layer-step with such splits, so they stay whole there.
+      // 71.2 us per layer-step unsplit against 77.3 (96-page pieces), 73.2 (64) and 77.4 (48),
+      // so they stay whole there.
       split = kMaxSplitPages;
       if (!has_tc) {
         int64_t pages = 0;
