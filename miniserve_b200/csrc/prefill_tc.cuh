@@ -143,10 +143,11 @@ __device__ __forceinline__ float max128(const float (&s0)[32], const float (&s1)
 }
 
 // p = 2^(s * scale_log2 - m) for 32 scores, accumulated into the pair sums and packed as 16 bf16
-// pairs.  Elements are processed in pairs with the paired fp32 instructions; 2 of every 8 pairs
-// go to the FMA pipe (exp2_fma2), which balances the MUFU pipe against instruction issue when two
-// softmax warps share a sub-partition (measured: 0, 2, 3, 4, 5 of 8 give 79.6, 76.3, 80.2, 82.8,
-// 86.0 us on a 4096-token prompt).  Masked scores (-inf) give 0 on either pipe, so blocks with and
+// pairs.  Elements are processed in pairs with the paired fp32 instructions; 1 of every 8 pairs
+// goes to the FMA pipe (exp2_fma2), which balances the MUFU pipe against instruction issue when
+// two softmax warps share a sub-partition (measured on the current kernel, 8192-token prompt: 1, 2
+// and 3 of 8 give 237.5, 245.7 and 255.3 us; config 3's chunks 27.4, 27.9 and 28.6 us; an earlier
+// form of the kernel, before the P halves and the early start, was fastest at 2 of 8).  Masked scores (-inf) give 0 on either pipe, so blocks with and
 // without masked scores run this same code: with a separate all-MUFU form for masked blocks, a
 // warpgroup in its diagonal block and the other warpgroup in an unmasked block ran two different
 // unrolled loops side by side, and the diagonal block took ~2.3x as long.
@@ -156,7 +157,7 @@ __device__ __forceinline__ void exp_pack32(const float (&sv)[32], float2 sc2, fl
   for (int i = 0; i < 16; ++i) {
     const float2 x = __ffma2_rn(make_float2(sv[2 * i], sv[2 * i + 1]), sc2, nm2);
     const float2 p =
-        (i & 7) < 2 ? exp2_fma2(x) : make_float2(fast_exp2(x.x), fast_exp2(x.y));
+        (i & 7) == 0 ? exp2_fma2(x) : make_float2(fast_exp2(x.x), fast_exp2(x.y));
     suma[i & 3] = __fadd2_rn(suma[i & 3], p);
     packed[i] = pack_bf16(p.x, p.y);
   }
