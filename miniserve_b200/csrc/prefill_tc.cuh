@@ -88,32 +88,6 @@ __device__ __forceinline__ void tma_load_5d_plain(void* smem_dst, const CUtensor
       : "memory");
 }
 
-// 2^x for two arguments on the FMA pipe instead of the MUFU unit (the softmax of a 128x128 score
-// block is MUFU-bound otherwise), with the paired fp32 instructions of sm_100 (one FFMA2 / FADD2
-// does both lanes), which makes it cheaper per element than the MUFU exponential.  Range
-// reduction x = n + f with n = round(x), f in [-1/2, 1/2]: adding 1.5 * 2^23 rounds x to an integer
-// held in the low mantissa bits, so no float-to-int conversion is needed.  2^f comes from a cubic
-// whose coefficients were fitted here for minimum relative error on [-1/2, 1/2] (max 7.5e-5, far
-// below the 2^-9 spacing of the bf16 P it feeds); 2^n is added to the exponent field.  Callers
-// pass x <= 8; below -126 (masked scores are -inf) the result is exactly 0, as ex2.approx.ftz
-// gives there.
-__device__ __forceinline__ float2 exp2_fma2(float2 xin) {
-  float2 x;
-  x.x = fmaxf(xin.x, -126.f);
-  x.y = fmaxf(xin.y, -126.f);
-  const float2 shifted = __fadd2_rn(x, make_float2(12582912.f, 12582912.f));
-  const float2 rounded = __fadd2_rn(shifted, make_float2(-12582912.f, -12582912.f));
-  const float2 f = __ffma2_rn(rounded, make_float2(-1.f, -1.f), x);
-  float2 p = __ffma2_rn(make_float2(0.0551716685295105f, 0.0551716685295105f), f,
-                        make_float2(0.2426111400127411f, 0.2426111400127411f));
-  p = __ffma2_rn(p, f, make_float2(0.6932609677314758f, 0.6932609677314758f));
-  p = __ffma2_rn(p, f, make_float2(0.9999280571937561f, 0.9999280571937561f));
-  const int nx = __float_as_int(shifted.x) - 0x4B400000;
-  const int ny = __float_as_int(shifted.y) - 0x4B400000;
-  return make_float2(xin.x < -126.f ? 0.f : __int_as_float(__float_as_int(p.x) + (nx << 23)),
-                     xin.y < -126.f ? 0.f : __int_as_float(__float_as_int(p.y) + (ny << 23)));
-}
-
 // Causal / range mask of 32 consecutive keys: key i is visible iff i < lim, where lim = (the
 // row's first invisible key, min(qpos + 1, key_end)) - (the first of the 32 keys).  Within a block
 // the invisible keys of a row are a suffix, so one compare with a constant and one select per
@@ -143,21 +117,20 @@ __device__ __forceinline__ float max128(const float (&s0)[32], const float (&s1)
 }
 
 // p = 2^(s * scale_log2 - m) for 32 scores, accumulated into the pair sums and packed as 16 bf16
-// pairs.  Elements are processed in pairs with the paired fp32 instructions; 1 of every 8 pairs
-// goes to the FMA pipe (exp2_fma2), which balances the MUFU pipe against instruction issue when
-// two softmax warps share a sub-partition (measured on the current kernel, 8192-token prompt: 1, 2
-// and 3 of 8 give 237.5, 245.7 and 255.3 us; config 3's chunks 27.4, 27.9 and 28.6 us; an earlier
-// form of the kernel, before the P halves and the early start, was fastest at 2 of 8).  Masked scores (-inf) give 0 on either pipe, so blocks with and
-// without masked scores run this same code: with a separate all-MUFU form for masked blocks, a
-// warpgroup in its diagonal block and the other warpgroup in an unmasked block ran two different
-// unrolled loops side by side, and the diagonal block took ~2.3x as long.
+// pairs, every exponential on the MUFU unit (scores scaled in pairs with the paired fp32
+// instructions).  Moving a share of the pairs to the FMA pipe (a cubic 2^f with exponent-field
+// scaling) paid off on an earlier form of this kernel (2 of 8 fastest there), but with the P
+// halves, the early start and the exact ring waits the MUFU-only form is the fastest: 0, 1, 2 and
+// 3 of 8 give 236.7, 237.5, 245.7 and 255.3 us on an 8192-token prompt.  Masked scores (-inf)
+// give 0, so blocks with and without masked scores run this same code: with a separate form for
+// masked blocks, a warpgroup in its diagonal block and the other warpgroup in an unmasked block
+// ran two different unrolled loops side by side, and the diagonal block took ~2.3x as long.
 __device__ __forceinline__ void exp_pack32(const float (&sv)[32], float2 sc2, float2 nm2,
                                            float2 (&suma)[4], uint32_t (&packed)[16]) {
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
     const float2 x = __ffma2_rn(make_float2(sv[2 * i], sv[2 * i + 1]), sc2, nm2);
-    const float2 p =
-        (i & 7) == 0 ? exp2_fma2(x) : make_float2(fast_exp2(x.x), fast_exp2(x.y));
+    const float2 p = make_float2(fast_exp2(x.x), fast_exp2(x.y));
     suma[i & 3] = __fadd2_rn(suma[i & 3], p);
     packed[i] = pack_bf16(p.x, p.y);
   }
