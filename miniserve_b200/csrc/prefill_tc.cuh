@@ -10,8 +10,8 @@
 //               224 registers each (the producer / MMA warpgroup gives its registers up).
 //               Per block: read the row's 128 scores from TMEM and release the S columns at once
 //               (the next S then runs on the tensor core during this block's softmax), causal /
-//               range mask (cached length as offset), row max, p = 2^(s*scale*log2e - m) (2 of 8
-//               pairs on the FMA pipe), row sum, and P packed to bf16 in registers; then, once
+//               range mask (cached length as offset), row max, p = 2^(s*scale*log2e - m) (MUFU),
+//               row sum, and P packed to bf16 in registers; then, once
 //               this tile's previous P*V has finished with its P buffer in shared memory, P is
 //               stored there.  The running max only moves (and O in TMEM is rescaled) when it
 //               grows by more than 2^8.
